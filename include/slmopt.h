@@ -1,0 +1,227 @@
+/*
+ * slmopt.h -- C ABI of the B200 optimizer step for python-slm's gqa-135m-v1.
+ *
+ * One opaque handle owns the optimizer state of one model replica (or one
+ * ZeRO-1 shard of it) in HBM, in the reference's PARAM-001 flat order:
+ *   master weights f32[P], first moments f32[P], second moments f32[P],
+ *   bf16 weight storage u16[P], and the tensor table {name, elements, decay}.
+ * Gradients are borrowed for the duration of a call (device pointer, or a host
+ * pointer that the call copies in).  All device work is issued on the stream
+ * the caller passes (NULL = the legacy default stream).  No exception crosses
+ * this boundary; every entry point returns an slm_status.
+ *
+ * Citations are to the dhilipsiva/python-slm sources (path:line) whose
+ * interface each entry point replaces.  No torch type appears here.
+ */
+#ifndef SLMOPT_H
+#define SLMOPT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SLMOPT_ABI_VERSION 1
+
+/* Status codes.  Each maps 1:1 onto a reference ProductError code
+ * (src/error.rs:16-93) and its category / process exit code (error.rs:85-93):
+ * Internal=1, Usage=2, Integrity=3, Environment=4, Gate=5. */
+typedef enum slm_status {
+    SLM_OK = 0,
+    /* Gate (5): src/model/oracle.rs:489-494, :499-503, :519-531, :544-552 */
+    SLM_ERR_MODEL_GRADIENT_NONFINITE = 10,
+    SLM_ERR_MODEL_GRADIENT_NORM_NONFINITE = 11,
+    SLM_ERR_MODEL_OPTIMIZER_INPUT_INVALID = 12,
+    SLM_ERR_MODEL_OPTIMIZER_RESULT_NONFINITE = 13,
+    /* Integrity (3): src/train/trainer.rs:240-273, :163-189, :102-119 */
+    SLM_ERR_P12_OPTIMIZER_GRADIENT_INVALID = 20,
+    SLM_ERR_P12_SCHEDULER_STATE_MISMATCH = 21,
+    SLM_ERR_P12_OPTIMIZER_STATE_INVALID = 22,
+    SLM_ERR_P12_UPDATE_INDEX_INVALID = 23,
+    SLM_ERR_P12_SCHEDULE_INDEX_INVALID = 24,
+    SLM_ERR_E1_PARAMETER_LAYOUT_MISMATCH = 25,       /* full_state.rs:218-236 */
+    SLM_ERR_E1_STATE_ARTIFACT_INVALID = 26,          /* full_state.rs:467-480 */
+    SLM_ERR_P12_OPTIMIZER_PARAMETER_DUPLICATE = 27,  /* trainer.rs:199-206 */
+    /* Usage (2) */
+    SLM_ERR_INVALID_ARGUMENT = 30,
+    SLM_ERR_SIZE_LIMIT = 31,
+    /* Environment (4) */
+    SLM_ERR_CUDA = 40,
+    SLM_ERR_OUT_OF_MEMORY = 41,
+    SLM_ERR_NCCL = 42,
+    SLM_ERR_TIMEOUT = 43,
+    SLM_ERR_NO_DEVICE = 44,
+    /* Internal (1) */
+    SLM_ERR_INTERNAL = 50
+} slm_status;
+
+/* The reference's ProductError.code string for a status, e.g.
+ * "MODEL_GRADIENT_NONFINITE"; "OK" for SLM_OK. */
+const char* slm_status_code_string(int status);
+/* The reference's exit code of the status's category (src/error.rs:85-93); 0 for SLM_OK. */
+int slm_status_category(int status);
+/* Human-readable detail of the last failure on this thread (never NULL). */
+const char* slm_last_error_message(void);
+int slm_abi_version(void);
+
+typedef struct slm_opt_handle slm_opt_handle;
+
+/* One row of the PARAM-001 tensor table (src/model/oracle.rs:177-275,
+ * src/train/full_state.rs:113-154).  weight_decay follows weight_decay_for
+ * (full_state.rs:179-181): 0 exactly for names ending in "norm.weight". */
+typedef struct slm_tensor_spec {
+    const char* name;
+    uint64_t elements;
+    uint32_t weight_decay;
+} slm_tensor_spec;
+
+/* Artifact roles of the five-artifact checkpoint (src/train/full_state.rs:27-36);
+ * the runtime JSON stays with the host. */
+typedef enum slm_role {
+    SLM_ROLE_PARAMETERS_BF16 = 0, /* model/parameters.bf16, u16 LE */
+    SLM_ROLE_MASTER_F32 = 1,      /* optimizer/master.f32 */
+    SLM_ROLE_MOMENT1_F32 = 2,     /* optimizer/adamw-m1.f32 */
+    SLM_ROLE_MOMENT2_F32 = 3      /* optimizer/adamw-m2.f32 */
+} slm_role;
+
+typedef enum slm_dtype { SLM_DTYPE_F32 = 0, SLM_DTYPE_BF16 = 1 } slm_dtype;
+typedef enum slm_memory { SLM_MEMORY_DEVICE = 0, SLM_MEMORY_HOST = 1 } slm_memory;
+typedef enum slm_nonfinite_policy {
+    SLM_NONFINITE_SKIP = 0,  /* skip the update, state bit-unchanged, halve a dynamic scale */
+    SLM_NONFINITE_ERROR = 1  /* reference behaviour: MODEL_GRADIENT_NONFINITE, state unchanged */
+} slm_nonfinite_policy;
+typedef enum slm_scale_mode {
+    SLM_SCALE_STATIC = 0,  /* divide by static_loss_scale (1 for plain fp32 gradients) */
+    SLM_SCALE_DYNAMIC = 1  /* divide by the handle's device-resident dynamic loss scale */
+} slm_scale_mode;
+
+/* Hyperparameters of one step.  The reference freezes them as constants
+ * (src/model/oracle.rs:469-484, src/train/trainer.rs:276); here they are
+ * explicit.  slm_step_config_default() fills OPT-001's values. */
+typedef struct slm_step_config {
+    float learning_rate;
+    uint32_t one_based_update;  /* t >= 1; bias corrections use f32 powi(beta, t) */
+    float beta1, beta2, epsilon;
+    float decay_weight;         /* for tensors with weight_decay=1 (0.1) */
+    float no_decay_weight;      /* for the RMSNorm scales (0.0) */
+    float max_grad_norm;        /* global L2 clip (1.0) */
+    int32_t apply_clip;         /* 1: g *= clip; 0: measure only (pre-clipped input) */
+    float min_clip_accept;      /* >0: reject (no update) when clip < this (0.95 verification) */
+    int32_t nonfinite_policy;   /* slm_nonfinite_policy */
+    int32_t loss_scale_mode;    /* slm_scale_mode */
+    float static_loss_scale;    /* divisor under SLM_SCALE_STATIC */
+    uint32_t growth_interval;   /* dynamic scale doubles after this many applied steps */
+} slm_step_config;
+
+typedef struct slm_step_result {
+    double sum_squares;        /* fixed-tree f64 sum of the unscaled gradients' squares */
+    double grad_norm;          /* sqrt(sum_squares) */
+    float clip_scale;          /* min(max_norm / sqrtf((float)sum), 1); 1 when the sum is 0 */
+    float loss_scale_used;
+    float next_loss_scale;
+    uint32_t skipped;          /* 1: no state was written */
+    uint32_t nonfinite;        /* 1: an unscaled gradient was inf/nan */
+    uint32_t result_nonfinite; /* 1: AdamW produced non-finite state */
+    uint32_t rejected;         /* 1: clip verification failed */
+    uint32_t good_steps;       /* dynamic scaler's consecutive applied steps */
+    int32_t status;            /* slm_status of the step */
+} slm_step_result;
+
+void slm_step_config_default(slm_step_config* cfg);
+
+/* ---- lifetime ------------------------------------------------------------- */
+
+/* Allocate the state for the tensor table on `device`; every buffer zeroed.
+ * Replaces CudaTrainerBackend::from_state / FullModelState::new
+ * (src/train/cuda_backend.rs:56-73, src/train/full_state.rs:206-245).
+ * Rejects empty tables, empty or duplicate names. */
+int slm_opt_create(const slm_tensor_spec* table, uint32_t n_tensors, int device,
+                   slm_opt_handle** out);
+int slm_opt_destroy(slm_opt_handle* h);
+uint64_t slm_opt_parameter_count(const slm_opt_handle* h);
+/* Human-readable detail of the handle's last failure (never NULL). */
+const char* slm_opt_last_error(const slm_opt_handle* h);
+
+/* Masters from host f32[P]; bf16 = RNE(master), moments zero, as
+ * FullModelState::initialize_canonical does (src/train/full_state.rs:259-291). */
+int slm_opt_init_master(slm_opt_handle* h, const float* master_host, void* stream);
+
+/* ---- checkpoint codec (src/train/full_state.rs:387-520) --------------------- */
+
+/* Copy one artifact out (D2H, little-endian flat bytes in PARAM-001 order).
+ * `bytes` must equal the artifact size (2P or 4P).  Synchronous. */
+int slm_opt_snapshot(slm_opt_handle* h, int role, void* host_dst, uint64_t bytes);
+/* Copy one artifact in (H2D).  Call slm_opt_validate_state after the last one. */
+int slm_opt_restore(slm_opt_handle* h, int role, const void* host_src, uint64_t bytes);
+/* AdamwParameterState::validate (src/train/trainer.rs:163-189) on the device:
+ * all master/m/v finite and bf16 == RNE(master), else
+ * SLM_ERR_P12_OPTIMIZER_STATE_INVALID.  Synchronous. */
+int slm_opt_validate_state(slm_opt_handle* h);
+/* Device address of one state buffer (for in-place use of the bf16 weights). */
+int slm_opt_device_buffer(slm_opt_handle* h, int role, void** out_device_ptr);
+
+/* CanonicalAdamw::state_sha256 (src/train/trainer.rs:297-320): validates, then
+ * SHA-256 over tag, name, decay, count, master, bf16, m, v per tensor.
+ * Synchronous; downloads the whole state.  Not on the step's timed path. */
+int slm_opt_state_sha256(slm_opt_handle* h, char out_hex[65]);
+
+/* ---- the step --------------------------------------------------------------- */
+
+/* Fused mixed-precision step: unscale -> non-finite check -> fixed-tree f64
+ * norm -> clip -> AdamW (fp32 master/m/v) -> bf16 weight copy, and the loss
+ * scaler.  Subsumes src/train/trainer.rs:884-904 plus
+ * CudaTrainerBackend::apply_update (src/train/cuda_backend.rs:240-258).
+ * `grads` holds P elements of `dtype` in `memory`.  If `out` is non-NULL the
+ * call waits for the stream and fills it (status included); if NULL the call
+ * only enqueues, and slm_opt_read_result() collects the result later.
+ * The skip path (non-finite gradient under SLM_NONFINITE_SKIP) is a success. */
+int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
+                 const slm_step_config* cfg, slm_step_result* out, void* stream);
+/* Wait for the handle's last enqueued step on its stream and return its result. */
+int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out);
+
+/* slm_opt_step split in its two device passes, both enqueue-only:
+ *   slm_opt_norm_pass   -- stage (host) gradients, unscale, non-finite check,
+ *                          fixed-tree norm, clip / skip decision, scaler update
+ *                          (the reference's trainer.rs:884-901);
+ *   slm_opt_update_pass -- AdamW + bf16 weight write over the gradients the
+ *                          norm pass saw (CanonicalAdamw's loop, trainer.rs:274-293).
+ * The gradient buffer must stay valid until the update pass has run; cfg must
+ * be the same for both.  Lets a caller overlap the norm pass with other work
+ * or time each pass with its own events. */
+int slm_opt_norm_pass(slm_opt_handle* h, const void* grads, int dtype, int memory,
+                      const slm_step_config* cfg, void* stream);
+int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* stream);
+
+/* The strict drop-in for TrainerBackend::apply_update (src/train/trainer.rs:512-518)
+ * as CudaTrainerBackend implements it (src/train/cuda_backend.rs:240-258 ->
+ * CanonicalAdamw::apply_normalized_clipped_gradients, trainer.rs:222-295):
+ * n must equal P (else P12_OPTIMIZER_GRADIENT_INVALID); non-finite gradients
+ * fail with MODEL_GRADIENT_NONFINITE; the clip is re-verified (tolerance 0.05,
+ * trainer.rs:161) over the fixed f64 tree; the lr must bit-equal
+ * canonical_learning_rate(t) (P12_SCHEDULER_STATE_MISMATCH); AdamW runs with
+ * OPT-001's constants and no further clip.  `grads_host` is host f32[n].
+ * valid_targets is accepted and unused, as in the reference.  If out_sha256
+ * is non-NULL it receives the post-update state SHA-256 (slow, off-path). */
+int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
+                         float learning_rate, uint64_t one_based_update,
+                         uint64_t valid_targets, char* out_sha256_hex65);
+
+/* ---- loss scaler ------------------------------------------------------------- */
+int slm_opt_set_loss_scale(slm_opt_handle* h, float scale, uint32_t good_steps);
+int slm_opt_get_loss_scale(slm_opt_handle* h, float* scale, uint32_t* good_steps);
+
+/* ---- lr schedule (host, scalar) ---------------------------------------------- */
+
+/* src/train/trainer.rs:102-119 canonical_learning_rate: bit-exact f32 result. */
+int slm_canonical_learning_rate(uint64_t one_based_update, float* out);
+/* The same warmup + cosine form over explicit constants. */
+int slm_schedule_learning_rate(uint64_t one_based_update, float peak, float minimum,
+                               uint64_t warmup, uint64_t total, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SLMOPT_H */

@@ -1,0 +1,496 @@
+// Optimizer-step kernels for sm_100a.
+//
+// The step is pure streaming arithmetic (no contraction), so the kernels are
+// bound by HBM bandwidth: 128-bit coalesced loads/stores, streaming cache
+// hints for the state that is touched once, f64 shuffle trees for the norm.
+//
+//   norm_partials_kernel  -- reads the gradient once, unscales, forms one f64
+//                            partial per 65,536-element chunk with the fixed
+//                            tree, flags non-finite values; its last block
+//                            (atomic completion counter, no spinning) reduces
+//                            the partials, computes the clip and the skip
+//                            decision and advances the dynamic loss scaler.
+//   adamw_update_kernel   -- persistent grid over 4,096-element tiles: unscale,
+//                            clip, AdamW (fp32 master/m/v), bf16 weight copy.
+//
+// Exactness: every f32 operation of the AdamW recurrence is an explicit
+// round-to-nearest intrinsic (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn), so
+// nothing is contracted into an FMA and the order is the reference's
+// (src/model/oracle.rs:536-543); the file is also built with --fmad=false.
+#include "slmopt_internal.h"
+
+namespace slmopt {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ bool finite_f32(float x) {
+  return (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u;
+}
+
+// Unscaling by s.  When s is a normal power of two whose reciprocal is also
+// normal, x * (1/s) and x / s are the same exact real rounded once, so the
+// multiply is bit-identical to the reference's true division; otherwise the
+// IEEE division is used.
+struct ScaleInfo {
+  float s;
+  float inv;
+  bool mul;
+};
+
+__device__ __forceinline__ ScaleInfo decode_scale(float s) {
+  const uint32_t b = __float_as_uint(s);
+  const uint32_t e = (b >> 23) & 0xffu;
+  ScaleInfo r;
+  r.s = s;
+  r.mul = ((b & 0x807fffffu) == 0u) && e >= 1u && e <= 253u;
+  r.inv = __uint_as_float(((254u - e) & 0xffu) << 23);
+  return r;
+}
+
+template <bool kMul>
+__device__ __forceinline__ float unscale(float x, const ScaleInfo& sc) {
+  if constexpr (kMul) {
+    return __fmul_rn(x, sc.inv);
+  } else {
+    return __fdiv_rn(x, sc.s);
+  }
+}
+
+__device__ __forceinline__ uint16_t bf16_rne_bits(float v) {
+  // src/model/oracle.rs:300-304: bits + 0x7fff + lowest kept bit, keep the top half.
+  const uint32_t b = __float_as_uint(v);
+  return static_cast<uint16_t>((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+
+// ---- gradient loads (8 elements as f32) ------------------------------------
+__device__ __forceinline__ void unpack_bf16x8(const uint4 r, float (&x)[8]) {
+  x[0] = __uint_as_float(r.x << 16);
+  x[1] = __uint_as_float(r.x & 0xffff0000u);
+  x[2] = __uint_as_float(r.y << 16);
+  x[3] = __uint_as_float(r.y & 0xffff0000u);
+  x[4] = __uint_as_float(r.z << 16);
+  x[5] = __uint_as_float(r.z & 0xffff0000u);
+  x[6] = __uint_as_float(r.w << 16);
+  x[7] = __uint_as_float(r.w & 0xffff0000u);
+}
+
+// Gradient load for the norm pass: default caching, so the tail of the gradient
+// read here can still be in L2 when the update pass starts.
+__device__ __forceinline__ void load_grad8(const float* __restrict__ g, uint64_t e0, uint64_t n,
+                                           float (&x)[8]) {
+  if (e0 + kVec <= n) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(g + e0));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(g + e0 + 4));
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) x[j] = (e0 + j < n) ? g[e0 + j] : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void load_grad8(const uint16_t* __restrict__ g, uint64_t e0,
+                                           uint64_t n, float (&x)[8]) {
+  if (e0 + kVec <= n) {
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(g + e0)), x);
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j)
+      x[j] = (e0 + j < n) ? __uint_as_float(static_cast<uint32_t>(g[e0 + j]) << 16) : 0.0f;
+  }
+}
+
+// ---- the fixed f64 tree -----------------------------------------------------
+// Folds one double per thread of a 256-thread block; result valid in thread 0.
+__device__ __forceinline__ double block_fold(double v, double* warp_sums) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(kFull, v, off));
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (lane == 0) warp_sums[warp] = v;
+  __syncthreads();
+  double r = 0.0;
+  if (threadIdx.x == 0) {
+    double w[kTreeThreads / 32];
+#pragma unroll
+    for (int i = 0; i < int(kTreeThreads / 32); ++i) w[i] = warp_sums[i];
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+#pragma unroll
+      for (int i = 0; i < off; ++i) w[i] = __dadd_rn(w[i], w[i + off]);
+    }
+    r = w[0];
+  }
+  __syncthreads();
+  return r;
+}
+
+template <typename GT, bool kMul>
+__device__ __forceinline__ double chunk_thread_sum(const GT* __restrict__ g, uint64_t base,
+                                                   uint64_t n, const ScaleInfo& sc) {
+  double acc = 0.0;
+#pragma unroll 8
+  for (uint32_t k = 0; k < kChunkIters; ++k) {
+    const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
+                        static_cast<uint64_t>(threadIdx.x) * kVec;
+    float x[kVec];
+    load_grad8(g, e0, n, x);
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+      const double d = static_cast<double>(unscale<kMul>(x[j], sc));
+      // d*d is exact in f64 (24-bit significands), so the FMA rounds once,
+      // exactly like acc + d*d.
+      acc = __fma_rn(d, d, acc);
+    }
+  }
+  return acc;
+}
+
+// Last block: reduce the partials, decide clip / skip, advance the scaler.
+__device__ void finalize_block(const double* partials, DeviceStepState* st, DeviceScaler* scaler,
+                               const FinalizeParams& fp, double* warp_sums) {
+  double v = 0.0;
+  for (uint32_t c = threadIdx.x; c < fp.total_chunks; c += kTreeThreads)
+    v = __dadd_rn(v, __ldcg(partials + c));
+  const double sum = block_fold(v, warp_sums);
+  if (threadIdx.x != 0) return;
+
+  const uint32_t nonfinite = atomicExch(&st->nonfinite_accum, 0u) != 0u ? 1u : 0u;
+  const float scale = fp.dynamic ? scaler->scale : fp.static_scale;
+  const float sumf = __double2float_rn(sum);
+  const bool norm_bad = !finite_f32(sumf);
+  float clip;
+  if (norm_bad) {
+    clip = 0.0f;
+  } else if (sumf == 0.0f) {
+    clip = 1.0f;
+  } else {
+    clip = __fdiv_rn(fp.max_grad_norm, __fsqrt_rn(sumf));
+    clip = clip < 1.0f ? clip : 1.0f;
+  }
+  st->sum_squares = sum;
+  st->grad_norm = __dsqrt_rn(sum);
+  st->clip_scale = clip;
+  st->clip_apply = fp.apply_clip ? clip : 1.0f;
+  st->loss_scale_used = scale;
+  st->nonfinite = nonfinite;
+  st->result_nonfinite = 0u;
+  st->rejected = 0u;
+  st->skipped = 0u;
+  st->status = kStatusOk;
+
+  float next = scale;
+  uint32_t good = fp.dynamic ? scaler->good_steps : 0u;
+  if (nonfinite || norm_bad) {
+    st->skipped = 1u;
+    if (fp.nonfinite_policy == 1)
+      st->status = nonfinite ? kStatusGradientNonfinite : kStatusNormNonfinite;
+    if (fp.dynamic) {
+      next = __fmul_rn(scale, 0.5f);
+      good = 0u;
+    }
+  } else if (fp.min_clip_accept > 0.0f && clip < fp.min_clip_accept) {
+    st->skipped = 1u;
+    st->rejected = 1u;
+    st->status = kStatusGradientInvalid;
+  } else if (fp.dynamic) {
+    good += 1u;
+    if (good >= fp.growth_interval) {
+      next = __fmul_rn(scale, 2.0f);
+      good = 0u;
+    }
+  }
+  if (fp.dynamic) {
+    scaler->scale = next;
+    scaler->good_steps = good;
+  }
+  st->next_loss_scale = next;
+  st->good_steps = good;
+  st->blocks_done = 0u;
+  __threadfence();
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kTreeThreads)
+    norm_partials_kernel(const GT* __restrict__ g, uint64_t n, uint64_t chunk_begin,
+                         uint32_t n_chunks, DeviceScaler* scaler, double* __restrict__ partials,
+                         DeviceStepState* st, FinalizeParams fp) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  __shared__ uint32_t s_last;
+  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
+  bool bad = false;
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint64_t chunk = chunk_begin + c;
+    const uint64_t base = chunk * kChunkElems;
+    // Squares are >= 0, so the partial is finite exactly when every unscaled
+    // element is finite (f32^2 * 65,536 cannot overflow f64).
+    const double acc = sc.mul ? chunk_thread_sum<GT, true>(g, base, n, sc)
+                              : chunk_thread_sum<GT, false>(g, base, n, sc);
+    bad |= !isfinite(acc);
+    const double total = block_fold(acc, warp_sums);
+    if (threadIdx.x == 0) partials[chunk] = total;
+  }
+  const int any_bad = __syncthreads_or(bad ? 1 : 0);
+  if (threadIdx.x == 0) {
+    if (any_bad) atomicOr(&st->nonfinite_accum, 1u);
+    __threadfence();
+    s_last = (atomicAdd(&st->blocks_done, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (s_last == 0u) return;
+  __threadfence();
+  finalize_block(partials, st, scaler, fp, warp_sums);
+}
+
+// ---- AdamW update -------------------------------------------------------------
+__device__ __forceinline__ float adamw_elem(float th, float gv, float& m, float& v, float wd,
+                                            const AdamwParams& p, bool& bad) {
+  const float m1 = __fadd_rn(__fmul_rn(p.beta1, m), __fmul_rn(p.omb1, gv));
+  const float v1 = __fadd_rn(__fmul_rn(p.beta2, v), __fmul_rn(__fmul_rn(p.omb2, gv), gv));
+  const float mh = __fdiv_rn(m1, p.bc1);
+  const float vh = __fdiv_rn(v1, p.bc2);
+  const float den = __fadd_rn(__fsqrt_rn(vh), p.eps);
+  const float upd = __fadd_rn(__fdiv_rn(mh, den), __fmul_rn(wd, th));
+  const float t1 = __fsub_rn(th, __fmul_rn(p.lr, upd));
+  bad |= !(finite_f32(m1) && finite_f32(v1) && finite_f32(t1));
+  m = m1;
+  v = v1;
+  return t1;
+}
+
+__device__ __forceinline__ void ld8_stream(const float* __restrict__ p, float (&x)[8]) {
+  const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldcs(reinterpret_cast<const float4*>(p + 4));
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ void st8_stream(float* __restrict__ p, const float (&x)[8]) {
+  __stcs(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+  __stcs(reinterpret_cast<float4*>(p + 4), make_float4(x[4], x[5], x[6], x[7]));
+}
+
+__device__ __forceinline__ void ld_grad8_stream(const float* __restrict__ g, float (&x)[8]) {
+  ld8_stream(g, x);
+}
+
+__device__ __forceinline__ void ld_grad8_stream(const uint16_t* __restrict__ g, float (&x)[8]) {
+  unpack_bf16x8(__ldcs(reinterpret_cast<const uint4*>(g)), x);
+}
+
+__device__ __forceinline__ float ld_grad1(const float* __restrict__ g, uint64_t i) { return g[i]; }
+__device__ __forceinline__ float ld_grad1(const uint16_t* __restrict__ g, uint64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(g[i]) << 16);
+}
+
+// Decay weight of global element e, scanning forward from tensor k.
+__device__ __forceinline__ float decay_of(uint64_t e, uint32_t& k,
+                                          const uint64_t* __restrict__ offsets,
+                                          const uint8_t* __restrict__ decay,
+                                          const AdamwParams& p) {
+  while (e >= __ldg(offsets + k + 1)) ++k;
+  return __ldg(decay + k) ? p.decay_weight : p.no_decay_weight;
+}
+
+template <typename GT, bool kMul>
+__device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n,
+                                            uint64_t elem_base, float* __restrict__ master,
+                                            float* __restrict__ mom, float* __restrict__ var,
+                                            uint16_t* __restrict__ w16,
+                                            const uint64_t* __restrict__ offsets,
+                                            const uint8_t* __restrict__ decay,
+                                            const uint32_t* __restrict__ tile_first,
+                                            const AdamwParams& p, const ScaleInfo& sc,
+                                            float clip) {
+  bool bad = false;
+  const uint64_t n_tiles = (n + kTileElems - 1) / kTileElems;
+  for (uint64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const uint32_t first = __ldg(tile_first + tile);
+    uint64_t i0[kUpdateUnroll];
+    bool full[kUpdateUnroll];
+    float gx[kUpdateUnroll][kVec], th[kUpdateUnroll][kVec], mm[kUpdateUnroll][kVec],
+        vv[kUpdateUnroll][kVec];
+    // Phase 1: issue every load of this tile before any arithmetic.
+#pragma unroll
+    for (uint32_t u = 0; u < kUpdateUnroll; ++u) {
+      i0[u] = tile * kTileElems + u * (kUpdateThreads * kVec) +
+              static_cast<uint64_t>(threadIdx.x) * kVec;
+      full[u] = i0[u] + kVec <= n;
+      if (full[u]) {
+        ld_grad8_stream(g + i0[u], gx[u]);
+        ld8_stream(master + i0[u], th[u]);
+        ld8_stream(mom + i0[u], mm[u]);
+        ld8_stream(var + i0[u], vv[u]);
+      }
+    }
+    // Phase 2: arithmetic and stores.
+#pragma unroll
+    for (uint32_t u = 0; u < kUpdateUnroll; ++u) {
+      uint32_t k = first;
+      if (full[u]) {
+        const uint64_t e0 = elem_base + i0[u];
+        const float wd0 = decay_of(e0, k, offsets, decay, p);
+        const bool uniform = e0 + kVec <= __ldg(offsets + k + 1);
+        uint32_t bits[kVec];
+#pragma unroll
+        for (uint32_t j = 0; j < kVec; ++j) {
+          const float wd = uniform ? wd0 : decay_of(e0 + j, k, offsets, decay, p);
+          const float gv = __fmul_rn(unscale<kMul>(gx[u][j], sc), clip);
+          th[u][j] = adamw_elem(th[u][j], gv, mm[u][j], vv[u][j], wd, p, bad);
+          bits[j] = bf16_rne_bits(th[u][j]);
+        }
+        st8_stream(master + i0[u], th[u]);
+        st8_stream(mom + i0[u], mm[u]);
+        st8_stream(var + i0[u], vv[u]);
+        uint4 packed;
+        packed.x = bits[0] | (bits[1] << 16);
+        packed.y = bits[2] | (bits[3] << 16);
+        packed.z = bits[4] | (bits[5] << 16);
+        packed.w = bits[6] | (bits[7] << 16);
+        __stcs(reinterpret_cast<uint4*>(w16 + i0[u]), packed);
+      } else if (i0[u] < n) {
+        // Ragged tail: scalar accesses for the last < 8 elements.
+        for (uint32_t j = 0; j < kVec && i0[u] + j < n; ++j) {
+          const uint64_t i = i0[u] + j;
+          const float wd = decay_of(elem_base + i, k, offsets, decay, p);
+          const float gv = __fmul_rn(unscale<kMul>(ld_grad1(g, i), sc), clip);
+          float m = mom[i], v = var[i];
+          const float t1 = adamw_elem(master[i], gv, m, v, wd, p, bad);
+          master[i] = t1;
+          mom[i] = m;
+          var[i] = v;
+          w16[i] = bf16_rne_bits(t1);
+        }
+      }
+    }
+  }
+  return bad;
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kUpdateThreads)
+    adamw_update_kernel(const GT* __restrict__ g, uint64_t n, uint64_t elem_base,
+                        float* __restrict__ master, float* __restrict__ mom,
+                        float* __restrict__ var, uint16_t* __restrict__ w16,
+                        const uint64_t* __restrict__ offsets, const uint8_t* __restrict__ decay,
+                        const uint32_t* __restrict__ tile_first, AdamwParams p,
+                        DeviceStepState* st) {
+  // Written by the previous kernel on this stream; uniform for the grid.
+  if (st->skipped) return;
+  const ScaleInfo sc = decode_scale(st->loss_scale_used);
+  const float clip = st->clip_apply;
+  const bool bad =
+      sc.mul ? update_loop<GT, true>(g, n, elem_base, master, mom, var, w16, offsets, decay,
+                                     tile_first, p, sc, clip)
+             : update_loop<GT, false>(g, n, elem_base, master, mom, var, w16, offsets, decay,
+                                      tile_first, p, sc, clip);
+  if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(&st->result_nonfinite, 1u);
+}
+
+// ---- state initialisation / validation ----------------------------------------
+__global__ void init_from_master_kernel(const float* __restrict__ master,
+                                        uint16_t* __restrict__ w16, uint64_t n) {
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+    w16[i] = bf16_rne_bits(master[i]);
+}
+
+__global__ void validate_state_kernel(const float* __restrict__ master,
+                                      const float* __restrict__ mom,
+                                      const float* __restrict__ var,
+                                      const uint16_t* __restrict__ w16, uint64_t n,
+                                      uint32_t* bad_flag) {
+  bool bad = false;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const float t = master[i];
+    bad |= !(finite_f32(t) && finite_f32(mom[i]) && finite_f32(var[i]) &&
+             bf16_rne_bits(t) == w16[i]);
+  }
+  if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(bad_flag, 1u);
+}
+
+int sm_count(int device) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      sms <= 0)
+    sms = 148;
+  return sms;
+}
+
+}  // namespace
+
+int norm_partials_grid(int device) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, norm_partials_kernel<uint16_t>,
+                                                    kTreeThreads, 0) != cudaSuccess ||
+      per_sm <= 0)
+    per_sm = 4;
+  return sm_count(device) * per_sm;
+}
+
+int adamw_update_grid(int device, int dtype) {
+  int per_sm = 0;
+  cudaError_t e =
+      dtype == 0 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                       &per_sm, adamw_update_kernel<float>, kUpdateThreads, 0)
+                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                       &per_sm, adamw_update_kernel<uint16_t>, kUpdateThreads, 0);
+  if (e != cudaSuccess || per_sm <= 0) per_sm = 2;
+  return sm_count(device) * per_sm;
+}
+
+cudaError_t launch_norm_partials(int dtype, const void* grads, uint64_t n, uint64_t chunk_begin,
+                                 uint32_t n_chunks, DeviceScaler* scaler, double* partials,
+                                 DeviceStepState* st, const FinalizeParams& fp, int grid,
+                                 cudaStream_t stream) {
+  if (n_chunks == 0) return cudaErrorInvalidValue;
+  const unsigned blocks = static_cast<unsigned>(grid < int(n_chunks) ? grid : int(n_chunks));
+  if (dtype == 0)
+    norm_partials_kernel<float><<<blocks, kTreeThreads, 0, stream>>>(
+        static_cast<const float*>(grads), n, chunk_begin, n_chunks, scaler, partials, st, fp);
+  else
+    norm_partials_kernel<uint16_t><<<blocks, kTreeThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(grads), n, chunk_begin, n_chunks, scaler, partials, st, fp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64_t elem_base,
+                                float* master, float* moment, float* variance, uint16_t* w16,
+                                const uint64_t* offsets, const uint8_t* decay,
+                                const uint32_t* tile_first_tensor, const AdamwParams& p,
+                                DeviceStepState* st, int grid, cudaStream_t stream) {
+  const uint64_t tiles = (n + kTileElems - 1) / kTileElems;
+  if (tiles == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>(uint64_t(grid) < tiles ? uint64_t(grid) : tiles);
+  if (dtype == 0)
+    adamw_update_kernel<float><<<blocks, kUpdateThreads, 0, stream>>>(
+        static_cast<const float*>(grads), n, elem_base, master, moment, variance, w16, offsets,
+        decay, tile_first_tensor, p, st);
+  else
+    adamw_update_kernel<uint16_t><<<blocks, kUpdateThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(grads), n, elem_base, master, moment, variance, w16,
+        offsets, decay, tile_first_tensor, p, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
+                                    uint64_t n, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(moment, 0, n * sizeof(float), stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(variance, 0, n * sizeof(float), stream);
+  if (e != cudaSuccess) return e;
+  init_from_master_kernel<<<sm_count(0) * 8, 256, 0, stream>>>(master, w16, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_validate_state(const float* master, const float* moment,
+                                  const float* variance, const uint16_t* w16, uint64_t n,
+                                  uint32_t* bad_flag, cudaStream_t stream) {
+  validate_state_kernel<<<sm_count(0) * 8, 256, 0, stream>>>(master, moment, variance, w16, n,
+                                                             bad_flag);
+  return cudaGetLastError();
+}
+
+}  // namespace slmopt

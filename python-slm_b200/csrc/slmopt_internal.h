@@ -1,0 +1,101 @@
+// Internal declarations shared by the kernels and the C-ABI host code.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace slmopt {
+
+// Fixed reduction tree of the global norm.  A chunk is 65,536 consecutive
+// elements of the flat PARAM-001 buffer; its f64 partial is formed by a
+// 256-thread block in which thread t owns, for k = 0..31, the 8 elements at
+// chunk_base + k*2048 + t*8 (squares added in that order), each warp folds with
+// shuffle offsets 16,8,4,2,1 and the 8 warp results fold with offsets 4,2,1.
+// The partials of all chunks are reduced by the same shape (thread t adds
+// partials t, t+256, ... in order).  The shape never depends on the grid, the
+// device, the gradient dtype or the number of ranks, so the norm is
+// bit-identical run to run, between the fp32 and bf16 paths and between one
+// GPU and a ZeRO-1 group.
+constexpr uint32_t kChunkElems = 65536;
+constexpr uint32_t kTreeThreads = 256;
+constexpr uint32_t kVec = 8;
+constexpr uint32_t kChunkIters = kChunkElems / (kTreeThreads * kVec);  // 32
+
+// Update kernel tiling: one 256-thread block step covers kTileElems elements.
+constexpr uint32_t kUpdateThreads = 256;
+constexpr uint32_t kUpdateUnroll = 2;
+constexpr uint32_t kTileElems = kUpdateThreads * kVec * kUpdateUnroll;  // 4096
+
+struct DeviceScaler {
+  float scale;
+  uint32_t good_steps;
+};
+
+// Step record in device memory.  The partial-sum kernel's last block fills it
+// (norm, clip, skip decision, scaler update); the update kernel reads it and
+// may set result_nonfinite; the host copies it out for slm_step_result.
+struct __align__(16) DeviceStepState {
+  double sum_squares;
+  double grad_norm;
+  float clip_scale;
+  float clip_apply;
+  float loss_scale_used;
+  float next_loss_scale;
+  uint32_t skipped;
+  uint32_t nonfinite;
+  uint32_t result_nonfinite;
+  uint32_t rejected;
+  uint32_t good_steps;
+  int32_t status;
+  // Accumulators owned by the partial-sum kernel, consumed and reset to zero by
+  // its last block, so every launch starts from zero without a memset.
+  uint32_t nonfinite_accum;
+  uint32_t blocks_done;
+};
+
+struct FinalizeParams {
+  float max_grad_norm;
+  float min_clip_accept;
+  int32_t apply_clip;
+  int32_t nonfinite_policy;  // 0 skip, 1 error
+  int32_t dynamic;           // read/update the device scaler
+  uint32_t growth_interval;
+  float static_scale;
+  uint32_t total_chunks;     // partials reduced by the finalize tree
+};
+
+struct AdamwParams {
+  float lr, beta1, beta2, omb1, omb2, bc1, bc2, eps, decay_weight, no_decay_weight;
+};
+
+// Status numbers mirrored from include/slmopt.h for device-side decisions.
+constexpr int32_t kStatusOk = 0;
+constexpr int32_t kStatusGradientNonfinite = 10;
+constexpr int32_t kStatusNormNonfinite = 11;
+constexpr int32_t kStatusResultNonfinite = 13;
+constexpr int32_t kStatusGradientInvalid = 20;
+
+// ---- launchers (kernels.cu) -------------------------------------------------
+// dtype: 0 = f32, 1 = bf16 (raw u16 bits).
+cudaError_t launch_norm_partials(int dtype, const void* grads, uint64_t n, uint64_t chunk_begin,
+                                 uint32_t n_chunks, DeviceScaler* scaler, double* partials,
+                                 DeviceStepState* st, const FinalizeParams& fp, int grid,
+                                 cudaStream_t stream);
+// Updates local elements [0, n); element i is global flat index elem_base + i
+// (the tensor table holds global offsets).  grads/master/moment/variance/w16
+// are all indexed by the local i.
+cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64_t elem_base,
+                                float* master, float* moment, float* variance, uint16_t* w16,
+                                const uint64_t* offsets, const uint8_t* decay,
+                                const uint32_t* tile_first_tensor, const AdamwParams& p,
+                                DeviceStepState* st, int grid, cudaStream_t stream);
+cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
+                                    uint64_t n, cudaStream_t stream);
+cudaError_t launch_validate_state(const float* master, const float* moment,
+                                  const float* variance, const uint16_t* w16, uint64_t n,
+                                  uint32_t* bad_flag, cudaStream_t stream);
+int norm_partials_grid(int device);
+int adamw_update_grid(int device, int dtype);
+
+}  // namespace slmopt

@@ -1,0 +1,416 @@
+"""CUDA path vs the CPU oracle, through the C ABI (libslmopt.so).
+
+Bar: bit-exact master / m / v / bf16 and bit-equal f64 norm, clip and skip
+decision on identical seeded inputs, from tiny ragged tables to the full
+135,285,504-parameter gqa-135m-v1 step (fp32 and bf16 gradients).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import slm_oracle as oracle
+from slmopt import B200Adamw, SlmError, StepOptions, TensorTable, _lib, synth
+from slmopt.layout import GqaDimensions
+
+pytestmark = pytest.mark.gpu
+
+THREADS = 8
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as _torch
+
+    if not _torch.cuda.is_available():
+        pytest.fail("a gpu-marked test ran without a CUDA device")
+    return _torch
+
+
+def assert_same_bits(got: np.ndarray, want: np.ndarray, what: str):
+    g = got.view(np.uint16 if got.dtype == np.uint16 else np.uint32)
+    w = want.view(np.uint16 if want.dtype == np.uint16 else np.uint32)
+    bad = np.flatnonzero(g != w)
+    assert bad.size == 0, (f"{what}: {bad.size} of {g.size} differ; first at {bad[0]}: "
+                           f"got {got[bad[0]]!r} want {want[bad[0]]!r}")
+
+
+def to_device(torch, grads: np.ndarray):
+    t = torch.from_numpy(grads)
+    return t.cuda()
+
+
+def oracle_config(opts: StepOptions):
+    return oracle.make_config(
+        lr=opts.learning_rate, t=opts.one_based_update, beta1=opts.beta1, beta2=opts.beta2,
+        eps=opts.epsilon, decay=opts.decay_weight, no_decay=opts.no_decay_weight,
+        max_norm=opts.max_grad_norm, apply_clip=opts.apply_clip,
+        min_clip_accept=opts.min_clip_accept, nonfinite_policy=opts.nonfinite_policy,
+        dynamic=opts.loss_scale_mode == _lib.SCALE_DYNAMIC,
+        static_scale=opts.static_loss_scale, growth_interval=opts.growth_interval)
+
+
+def run_both(torch, table: TensorTable, grads: np.ndarray, opts: StepOptions, seed: int = 0,
+             state: dict | None = None, host_grads: bool = False):
+    n = table.parameter_count
+    state = state if state is not None else synth.optimizer_state(n, seed)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        g = grads if host_grads else to_device(torch, grads)
+        res = opt.step(g, opts)
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in state.items()}
+    ores = oracle.step(oracle_config(opts), grads, table.offsets, table.decay, ost,
+                       threads=THREADS)
+    return res, got, ores, ost
+
+
+def check_equal(res, got, ores, ost):
+    assert res.skipped == ores.skipped
+    assert res.nonfinite == ores.nonfinite
+    assert res.status == ores.status
+    if not ores.nonfinite:
+        assert res.sum_squares == ores.sum_squares
+        assert res.grad_norm == ores.grad_norm
+        assert np.float32(res.clip_scale) == np.float32(ores.clip_scale)
+    assert res.loss_scale_used == ores.loss_scale_used
+    assert res.next_loss_scale == ores.next_loss_scale
+    for key in ("master", "moment", "variance", "bf16"):
+        assert_same_bits(got[key], ost[key], key)
+
+
+SMALL = [[1], [3, 5], [7, 9, 11, 4095], [65536, 5, 70000], [768] * 7 + [131075],
+         [2048 * 3 + 1, 13, 65536 * 2 + 8]]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("sizes", SMALL, ids=lambda s: f"{len(s)}t{sum(s)}")
+def test_small_tables_bit_exact(torch, dtype, sizes):
+    rng = np.random.default_rng(len(sizes))
+    table = TensorTable.from_sizes(sizes, rng.integers(0, 2, len(sizes)).astype(bool))
+    n = table.parameter_count
+    scale = 65536.0 if dtype == "bf16" else 1.0
+    grads = synth.grads_bf16(n, 5) if dtype == "bf16" else synth.grads_f32(n, 5)
+    opts = StepOptions(learning_rate=3e-4, one_based_update=10, static_loss_scale=scale)
+    check_equal(*run_both(torch, table, grads, opts, seed=5))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_clipped_step_bit_exact(torch, dtype):
+    table = TensorTable.from_sizes([300_001, 77, 5000], [True, False, True])
+    n = table.parameter_count
+    if dtype == "bf16":
+        grads = synth.grads_bf16(n, 8, loss_scale=65536.0 * 40)
+        opts = StepOptions(one_based_update=3, static_loss_scale=65536.0)
+    else:
+        grads = (synth.grads_f32(n, 8) * np.float32(40.0)).astype(np.float32)
+        opts = StepOptions(one_based_update=3)
+    res, got, ores, ost = run_both(torch, table, grads, opts, seed=8)
+    assert ores.clip_scale < 1.0
+    check_equal(res, got, ores, ost)
+
+
+def test_non_power_of_two_scale_uses_true_division(torch):
+    # The reference's final update normalises by 37,888 targets (trainer.rs:15).
+    table = TensorTable.from_sizes([100_003])
+    n = table.parameter_count
+    grads = synth.grads_f32(n, 9) * np.float32(37888.0)
+    opts = StepOptions(one_based_update=30518, static_loss_scale=37888.0)
+    check_equal(*run_both(torch, table, grads.astype(np.float32), opts, seed=9))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_smoke_model_step_bit_exact(torch, dtype):
+    # config 0's tensor list (model-smoke.example.json, tied: 20 tensors) on the GPU
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    n = table.parameter_count
+    assert n == 4_489_856
+    scale = 65536.0 if dtype == "bf16" else 1.0
+    grads = synth.grads_bf16(n, 0) if dtype == "bf16" else synth.grads_f32(n, 0)
+    opts = StepOptions(learning_rate=3e-4, one_based_update=10, static_loss_scale=scale)
+    check_equal(*run_both(torch, table, grads, opts, seed=0))
+
+
+def test_135m_fp32_step_bit_exact(torch):
+    # config 1: gqa-135m-v1, fp32 gradients, t = 10
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    n = table.parameter_count
+    grads = synth.grads_f32(n, 0)
+    opts = StepOptions(learning_rate=3e-4, one_based_update=10)
+    res, got, ores, ost = run_both(torch, table, grads, opts, seed=0)
+    check_equal(res, got, ores, ost)
+    # the fixed tree is within 1e-6 relative of an f64 sequential sum
+    g = grads.astype(np.float64)
+    seq = float(np.dot(g, g))
+    assert abs(res.sum_squares - seq) <= 1e-6 * seq
+
+
+def test_135m_bf16_step_and_inf_skip(torch):
+    # config 2: bf16 gradients * 65536, dynamic scale; then one injected +inf
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    n = table.parameter_count
+    state = synth.optimizer_state(n, 0)
+    grads = synth.grads_bf16(n, 0)
+    opts = StepOptions(learning_rate=3e-4, one_based_update=10,
+                       loss_scale_mode=_lib.SCALE_DYNAMIC)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        opt.set_loss_scale(65536.0)
+        res = opt.step(to_device(torch, grads), opts)
+        got = opt.read_state()
+        ost = {k: v.copy() for k, v in state.items()}
+        scaler = oracle.Scaler(65536.0, 0)
+        ores = oracle.step(oracle_config(opts), grads, table.offsets, table.decay, ost, scaler,
+                           threads=THREADS)
+        check_equal(res, got, ores, ost)
+        assert res.skipped == 0 and opt.loss_scale() == (65536.0, 1)
+
+        bad = grads.copy()
+        k, i = synth.inject_nonfinite(bad, 1, table.offsets)
+        res2 = opt.step(to_device(torch, bad), StepOptions(
+            learning_rate=3e-4, one_based_update=11, loss_scale_mode=_lib.SCALE_DYNAMIC))
+        after = opt.read_state()
+        assert res2.skipped == 1 and res2.nonfinite == 1 and res2.status == 0
+        assert res2.loss_scale_used == 65536.0 and res2.next_loss_scale == 32768.0
+        assert opt.loss_scale() == (32768.0, 0)
+        for key in got:
+            assert_same_bits(after[key], got[key], key + " after skip")
+
+
+def test_runs_are_bit_identical(torch):
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    n = table.parameter_count
+    grads = synth.grads_bf16(n, 2)
+    opts = StepOptions(one_based_update=10, static_loss_scale=65536.0)
+    outs = []
+    for _ in range(2):
+        res, got, _, _ = run_both(torch, table, grads, opts, seed=2)
+        outs.append((res.sum_squares, got))
+    assert outs[0][0] == outs[1][0]
+    for key in outs[0][1]:
+        assert_same_bits(outs[0][1][key], outs[1][1][key], key)
+
+
+def test_host_gradients_equal_device_gradients(torch):
+    table = TensorTable.from_sizes([70_000, 33])
+    n = table.parameter_count
+    grads = synth.grads_bf16(n, 4)
+    opts = StepOptions(one_based_update=2, static_loss_scale=65536.0)
+    r1, g1, _, _ = run_both(torch, table, grads, opts, seed=4)
+    r2, g2, _, _ = run_both(torch, table, grads, opts, seed=4, host_grads=True)
+    assert r1.sum_squares == r2.sum_squares
+    for key in g1:
+        assert_same_bits(g1[key], g2[key], key)
+
+
+def test_async_step_on_a_stream_then_read_result(torch):
+    table = TensorTable.from_sizes([123_457])
+    n = table.parameter_count
+    state = synth.optimizer_state(n, 6)
+    grads = synth.grads_f32(n, 6)
+    s = torch.cuda.Stream()
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        with torch.cuda.stream(s):
+            dev = to_device(torch, grads)
+        assert opt.step(dev, StepOptions(one_based_update=4), stream=s, wait=False) is None
+        res = opt.read_result()
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in state.items()}
+    ores = oracle.step(oracle.make_config(t=4), grads, table.offsets, table.decay, ost)
+    check_equal(res, got, ores, ost)
+
+
+def test_misaligned_device_gradients_are_rejected(torch):
+    table = TensorTable.from_sizes([64])
+    buf = torch.zeros(65, dtype=torch.float32, device="cuda")
+    with B200Adamw(table) as opt:
+        with pytest.raises(SlmError) as e:
+            opt.step(buf[1:], StepOptions())
+        assert e.value.code == "SLM_INVALID_ARGUMENT"
+
+
+def test_error_policy_leaves_state_unchanged(torch):
+    table = TensorTable.from_sizes([5000, 100], [True, False])
+    n = table.parameter_count
+    state = synth.optimizer_state(n, 3)
+    grads = synth.grads_f32(n, 3)
+    grads[4321] = np.nan
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        with pytest.raises(SlmError) as e:
+            opt.step(to_device(torch, grads), StepOptions(nonfinite_policy=_lib.NONFINITE_ERROR))
+        assert e.value.code == "MODEL_GRADIENT_NONFINITE" and e.value.category == 5
+        got = opt.read_state()
+    for key in got:
+        assert_same_bits(got[key], state[key], key)
+
+
+# ---- strict TrainerBackend::apply_update drop-in ------------------------------------
+def test_apply_update_two_parameter_canonical_adamw(torch):
+    # tests/p12_trainer.rs:331-362 through the C ABI, hashed like trainer.rs:297-320
+    table = TensorTable(names=("matrix.weight", "norm.weight"), shapes=((1,), (1,)),
+                        elements=(1, 1), decay=(True, False))
+    st0 = {"master": np.ones(2, np.float32), "moment": np.zeros(2, np.float32),
+           "variance": np.zeros(2, np.float32), "bf16": np.full(2, 0x3F80, np.uint16)}
+    lr = oracle.canonical_learning_rate(1)[1]
+    with B200Adamw(table) as opt:
+        opt.load_state(st0["master"], st0["moment"], st0["variance"], st0["bf16"])
+        before = opt.state_sha256()
+        after = opt.apply_normalized_clipped_gradients(np.array([0.5, 0.5], np.float32), lr, 1)
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in st0.items()}
+    assert oracle.apply_normalized_clipped_gradients(
+        np.array([0.5, 0.5], np.float32), lr, 1, table.offsets, table.decay, ost)[0] == 0
+    assert oracle.state_sha256(table.names, table.offsets, table.decay, st0)[1] == before
+    assert oracle.state_sha256(table.names, table.offsets, table.decay, ost)[1] == after
+    assert before != after
+    assert got["master"][0] < got["master"][1]
+    for key in got:
+        assert_same_bits(got[key], ost[key], key)
+
+
+def test_apply_update_rejections_match_reference(torch):
+    table = TensorTable.from_sizes([1000, 24], [True, False])
+    n = table.parameter_count
+    state = synth.optimizer_state(n, 1)
+    lr1 = oracle.canonical_learning_rate(1)[1]
+    small = (synth.grads_f32(n, 1) * np.float32(0.01)).astype(np.float32)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        cases = [
+            (small[:-1], lr1, 1, "P12_OPTIMIZER_GRADIENT_INVALID"),
+            (np.where(np.arange(n) == 7, np.float32(np.inf), small).astype(np.float32), lr1, 1,
+             "MODEL_GRADIENT_NONFINITE"),
+            ((small * np.float32(1e4)).astype(np.float32), lr1, 1, "P12_OPTIMIZER_GRADIENT_INVALID"),
+            (small, lr1, 1 << 33, "P12_UPDATE_INDEX_INVALID"),
+            (small, lr1, 0, "P12_SCHEDULE_INDEX_INVALID"),
+            (small, 3e-4, 1, "P12_SCHEDULER_STATE_MISMATCH"),
+        ]
+        for g, lr, t, code in cases:
+            with pytest.raises(SlmError) as e:
+                opt.apply_normalized_clipped_gradients(g, lr, t, with_sha=False)
+            assert e.value.code == code
+            if len(g) == n:
+                ost = {k: v.copy() for k, v in state.items()}
+                assert oracle.apply_normalized_clipped_gradients(
+                    g, lr, t, table.offsets, table.decay, ost)[0] == getattr(oracle, code)
+        got = opt.read_state()
+    for key in got:
+        assert_same_bits(got[key], state[key], key)
+
+
+def test_apply_update_matches_oracle_over_steps(torch):
+    table = TensorTable.from_dimensions(GqaDimensions.oracle_fixture())
+    n = table.parameter_count
+    master = synth.bf16_bits_to_f32(synth.bf16_rne_bits(synth.normal_f32(n, 0.02, 7, 1)))
+    st = {"master": master.copy(), "moment": np.zeros(n, np.float32),
+          "variance": np.zeros(n, np.float32), "bf16": synth.bf16_rne_bits(master)}
+    ost = {k: v.copy() for k, v in st.items()}
+    with B200Adamw(table) as opt:
+        opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+        for t in range(1, 6):
+            g = np.where(np.arange(n) % 3 == 0, np.float32(0.01 * t),
+                         np.float32(-0.004)).astype(np.float32)
+            lr = oracle.canonical_learning_rate(t)[1]
+            sha = opt.apply_normalized_clipped_gradients(g, lr, t)
+            assert oracle.apply_normalized_clipped_gradients(
+                g, lr, t, table.offsets, table.decay, ost)[0] == 0
+            assert sha == oracle.state_sha256(table.names, table.offsets, table.decay, ost)[1]
+
+
+# ---- codec ------------------------------------------------------------------------------
+def test_snapshot_restore_round_trip(torch):
+    from slmopt import B200TrainerBackend
+
+    dims = GqaDimensions.oracle_fixture()
+    be = B200TrainerBackend(dims)
+    n = be.optimizer.P
+    master = synth.normal_f32(n, 0.02, 1, 1)
+    be.optimizer.init_master(master)
+    lr = oracle.canonical_learning_rate(1)[1]
+    g = np.where(np.arange(n) % 3 == 0, np.float32(0.01), np.float32(-0.004)).astype(np.float32)
+    updated = be.apply_update(g, lr, 1, 65536)
+    arts = be.snapshot()
+    assert [a[0] for a in arts] == ["parameters_bf16", "master_parameters_fp32",
+                                    "adamw_first_moments_fp32", "adamw_second_moments_fp32"]
+    assert len(arts[0][2]) == 2 * n and all(len(a[2]) == 4 * n for a in arts[1:])
+    be2 = B200TrainerBackend(dims)
+    be2.restore(arts)
+    assert be2.state_sha256() == updated
+    assert be2.snapshot() == arts
+    bad = [(r, p, b) for r, p, b in arts if r != "adamw_first_moments_fp32"]
+    with pytest.raises(SlmError) as e:
+        be2.restore(bad)
+    assert e.value.code == "E1_STATE_ARTIFACT_INVALID"
+    truncated = [(r, p, b[:-4] if r == "master_parameters_fp32" else b) for r, p, b in arts]
+    with pytest.raises(SlmError) as e:
+        be2.restore(truncated)
+    assert e.value.code == "E1_STATE_ARTIFACT_INVALID"
+
+
+def test_validate_rejects_inconsistent_state(torch):
+    table = TensorTable.from_sizes([100])
+    st = synth.optimizer_state(100, 1)
+    bf = st["bf16"].copy()
+    bf[50] ^= 1
+    with B200Adamw(table) as opt:
+        with pytest.raises(SlmError) as e:
+            opt.load_state(st["master"], st["moment"], st["variance"], bf)
+        assert e.value.code == "P12_OPTIMIZER_STATE_INVALID"
+        m = st["moment"].copy()
+        m[3] = np.inf
+        with pytest.raises(SlmError):
+            opt.load_state(st["master"], m, st["variance"], st["bf16"])
+
+
+# ---- 100-step trajectory (config 4 at the smoke tensor list) ------------------------------
+def test_stress_trajectory_bit_exact_and_repeatable(torch):
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    n = table.parameter_count
+    steps = 100
+    inject = {17, 63}
+
+    def run_gpu():
+        st = synth.optimizer_state(n, 0)
+        results = []
+        with B200Adamw(table) as opt:
+            opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+            opt.set_loss_scale(65536.0)
+            scale = 65536.0
+            for t in range(1, steps + 1):
+                g = synth.grads_student_t(n, 0, t)
+                bits = synth.bf16_rne_bits((g * np.float32(scale)).astype(np.float32))
+                if t in inject:
+                    synth.inject_nonfinite(bits, t, table.offsets)
+                lr = oracle.schedule_learning_rate(t, 3e-4, 3e-5, 20, 100)[1]
+                r = opt.step(to_device(torch, bits), StepOptions(
+                    learning_rate=lr, one_based_update=t, loss_scale_mode=_lib.SCALE_DYNAMIC))
+                results.append((r.skipped, r.sum_squares, r.clip_scale, r.next_loss_scale))
+                scale = r.next_loss_scale
+            return results, opt.read_state()
+
+    res_a, state_a = run_gpu()
+    res_b, state_b = run_gpu()
+    assert res_a == res_b
+    for key in state_a:
+        assert_same_bits(state_a[key], state_b[key], key)
+
+    ost = synth.optimizer_state(n, 0)
+    scaler = oracle.Scaler(65536.0, 0)
+    for t in range(1, steps + 1):
+        g = synth.grads_student_t(n, 0, t)
+        bits = synth.bf16_rne_bits((g * np.float32(scaler.scale)).astype(np.float32))
+        if t in inject:
+            synth.inject_nonfinite(bits, t, table.offsets)
+        lr = oracle.schedule_learning_rate(t, 3e-4, 3e-5, 20, 100)[1]
+        r = oracle.step(oracle.make_config(lr=lr, t=t, dynamic=True), bits, table.offsets,
+                        table.decay, ost, scaler, threads=THREADS)
+        skipped, s, c, nxt = res_a[t - 1]
+        assert skipped == r.skipped, t
+        if not r.skipped:
+            assert s == r.sum_squares and np.float32(c) == np.float32(r.clip_scale), t
+        assert nxt == r.next_loss_scale
+    assert sum(x[0] for x in res_a) == len(inject)
+    for key in state_a:
+        assert_same_bits(state_a[key], ost[key], key)

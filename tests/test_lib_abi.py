@@ -1,0 +1,103 @@
+"""The C-ABI library loads, exports every declared entry point, and its host-only
+functions (status mapping, defaults, lr schedule) agree with the oracle.
+No kernel is launched here; these run without a GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import slm_oracle as oracle
+from slmopt import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions() -> list[str]:
+    text = (ROOT / "include" / "slmopt.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(slm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), name
+    bound = {n for n, _, _ in _lib.SIGNATURES}
+    assert set(names) <= bound | {"slm_opt_handle"}, set(names) - bound
+
+
+def test_status_codes_and_categories():
+    lib = _lib.load()
+    expect = {
+        0: ("OK", 0),
+        10: ("MODEL_GRADIENT_NONFINITE", 5),
+        11: ("MODEL_GRADIENT_NORM_NONFINITE", 5),
+        12: ("MODEL_OPTIMIZER_INPUT_INVALID", 5),
+        13: ("MODEL_OPTIMIZER_RESULT_NONFINITE", 5),
+        20: ("P12_OPTIMIZER_GRADIENT_INVALID", 3),
+        21: ("P12_SCHEDULER_STATE_MISMATCH", 3),
+        22: ("P12_OPTIMIZER_STATE_INVALID", 3),
+        23: ("P12_UPDATE_INDEX_INVALID", 3),
+        24: ("P12_SCHEDULE_INDEX_INVALID", 3),
+        26: ("E1_STATE_ARTIFACT_INVALID", 3),
+        30: ("SLM_INVALID_ARGUMENT", 2),
+        40: ("SLM_CUDA_ERROR", 4),
+        43: ("SLM_TIMEOUT", 4),
+        50: ("SLM_INTERNAL_ERROR", 1),
+    }
+    for status, (code, cat) in expect.items():
+        assert lib.slm_status_code_string(status).decode() == code
+        assert lib.slm_status_category(status) == cat
+    # oracle and product share the numbering
+    assert oracle.MODEL_GRADIENT_NONFINITE == _lib.SLM_ERR_MODEL_GRADIENT_NONFINITE
+    assert oracle.P12_SCHEDULER_STATE_MISMATCH == _lib.SLM_ERR_P12_SCHEDULER_STATE_MISMATCH
+
+
+def test_struct_layouts_match_oracle():
+    assert ctypes.sizeof(_lib.StepConfig) == ctypes.sizeof(oracle.StepConfig) == 56
+    assert ctypes.sizeof(_lib.StepResult) == ctypes.sizeof(oracle.StepResult)
+    assert [f for f, _ in _lib.StepResult._fields_] == [f for f, _ in oracle.StepResult._fields_]
+
+
+def test_learning_rate_schedules_bit_equal_to_oracle():
+    lib = _lib.load()
+    out = ctypes.c_float()
+    for t in list(range(1, 2001)) + list(range(2001, 30519, 97)) + [30518]:
+        st = lib.slm_canonical_learning_rate(t, ctypes.byref(out))
+        ost, olr = oracle.canonical_learning_rate(t)
+        assert st == ost == 0
+        assert struct.pack("<f", out.value) == struct.pack("<f", olr), t
+    assert lib.slm_canonical_learning_rate(0, ctypes.byref(out)) == \
+        _lib.SLM_ERR_P12_SCHEDULE_INDEX_INVALID
+    assert lib.slm_canonical_learning_rate(30519, ctypes.byref(out)) == \
+        _lib.SLM_ERR_P12_SCHEDULE_INDEX_INVALID
+    for t in range(1, 101):
+        st = lib.slm_schedule_learning_rate(t, 3e-4, 3e-5, 20, 100, ctypes.byref(out))
+        assert st == 0
+        assert np.float32(out.value) == np.float32(oracle.schedule_learning_rate(
+            t, 3e-4, 3e-5, 20, 100)[1])
+
+
+def test_create_without_device_fails_cleanly():
+    from conftest import have_gpu
+
+    if have_gpu():
+        pytest.skip("a GPU is visible")
+    from slmopt import B200Adamw, SlmError, TensorTable
+
+    with pytest.raises(SlmError) as e:
+        B200Adamw(TensorTable.from_sizes([8]))
+    assert e.value.code == "SLM_NO_DEVICE" and e.value.category == 4
+
+
+def test_create_rejects_bad_tables_before_touching_a_device():
+    lib = _lib.load()
+    h = ctypes.c_void_p()
+    assert lib.slm_opt_create(None, 0, 0, ctypes.byref(h)) == _lib.SLM_ERR_P12_OPTIMIZER_STATE_INVALID

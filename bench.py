@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["mixed", "fp32"], default="mixed")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--params", type=int, default=0,
+                    help="profiling only: run on the first N parameters (whole 65,536-element "
+                         "chunks) of the 135M layout instead of all of it")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -149,6 +152,26 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(max_sm) if max_sm else None,
                 "reasons": reasons, "samples": len(rows)}
+
+
+def prefix_table(table, n: int):
+    """The first n parameters (rounded down to whole chunks) of a tensor table."""
+    import numpy as np
+
+    from slmopt import TensorTable
+
+    n = max(65536, n // 65536 * 65536)
+    names, shapes, elems, decay = [], [], [], []
+    for name, shape, e, d, lo in zip(table.names, table.shapes, table.elements, table.decay,
+                                     table.offsets[:-1]):
+        if lo >= n:
+            break
+        take = int(min(e, n - lo))
+        names.append(name)
+        shapes.append(shape if take == e else (take,))
+        elems.append(take)
+        decay.append(d)
+    return TensorTable(tuple(names), tuple(shapes), tuple(elems), tuple(decay))
 
 
 def gpu_smi_id(device: int) -> str:
@@ -256,6 +279,8 @@ def run_single(args) -> None:
 
     torch.cuda.set_device(0)
     table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    if args.params:
+        table = prefix_table(table, args.params)
     P = table.parameter_count
     state = synth.optimizer_state(P, 0)
     mixed = args.workload == "mixed"

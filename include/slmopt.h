@@ -209,6 +209,31 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
                          float learning_rate, uint64_t one_based_update,
                          uint64_t valid_targets, char* out_sha256_hex65);
 
+/* ---- ZeRO-1 data parallel (no counterpart in the reference, which runs one
+ * device per process, src/train/cuda_backend.rs:56-73) ---------------------------
+ * One handle per rank and GPU.  The flat buffer is cut into 65,536-element
+ * chunks, the chunk count padded to a multiple of `world`; rank r owns the
+ * chunk-aligned element range slm_opt_shard_range() reports and keeps master /
+ * m / v for it, plus the full bf16 weights.  slm_opt_step() on such a handle
+ * takes this rank's full local gradient (P elements) and runs: all-to-all of
+ * gradient slices, f32 sum in rank order 0..N-1 fused with the unscale and the
+ * norm partials, all-gather of the partials, the same fixed-tree finalize on
+ * every rank, AdamW on the shard, in-place all-gather of the bf16 weights.
+ * The result equals a single replica's step on the rank-ordered f32 sum of the
+ * gradients, bit for bit.  Collective entry points (every rank calls them in
+ * the same order): slm_opt_create_zero1, slm_opt_step, slm_opt_init_master,
+ * slm_opt_snapshot of a full f32 role, slm_opt_state_sha256.  Waits are
+ * bounded by timeout_ms (0 = 300 s); on expiry the communicator is aborted and
+ * the call returns SLM_ERR_TIMEOUT. */
+
+/* A fresh NCCL unique id (128 bytes) for rank 0 to share with the others. */
+int slm_zero1_unique_id(uint8_t out[128]);
+int slm_opt_create_zero1(const slm_tensor_spec* table, uint32_t n_tensors, int device, int rank,
+                         int world, const uint8_t unique_id[128], uint32_t timeout_ms,
+                         slm_opt_handle** out);
+/* This rank's element range [begin, begin + len) of the flat buffer. */
+int slm_opt_shard_range(const slm_opt_handle* h, uint64_t* begin, uint64_t* len);
+
 /* ---- loss scaler ------------------------------------------------------------- */
 int slm_opt_set_loss_scale(slm_opt_handle* h, float scale, uint32_t good_steps);
 int slm_opt_get_loss_scale(slm_opt_handle* h, float* scale, uint32_t* good_steps);

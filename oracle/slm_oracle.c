@@ -379,6 +379,51 @@ void slmo_rank_sum_bf16(const uint16_t* const* grads, uint32_t ranks, uint64_t n
     }
 }
 
+/* AdamW over local elements [0, n) whose global flat indices start at
+ * elem_base (the decay weight comes from the global tensor table): unscale
+ * g_raw by `scale` (true division), multiply by `clip` when cfg->apply_clip,
+ * then src/model/oracle.rs:536-543 and bf16 storage.  Returns nonzero when any
+ * output is non-finite.  This is the update half of the fused step; a ZeRO-1
+ * rank runs it over its shard with the group's clip. */
+int slmo_adamw_apply_range(const slmo_step_config* cfg, const float* g_raw, uint64_t n,
+                           uint64_t elem_base, const uint64_t* tensor_offsets,
+                           const uint8_t* tensor_decay, uint32_t n_tensors, float scale,
+                           float clip, float* master, float* moment, float* variance,
+                           uint16_t* bf16, int threads) {
+    const float b1 = cfg->beta1, b2 = cfg->beta2, eps = cfg->epsilon;
+    const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
+    const float bc1 = 1.0f - slmo_powi(b1, (int32_t)cfg->one_based_update);
+    const float bc2 = 1.0f - slmo_powi(b2, (int32_t)cfg->one_based_update);
+    const float lr = cfg->learning_rate;
+    const float use_clip = cfg->apply_clip ? clip : 1.0f;
+    if (threads < 1) threads = 1;
+    int any_bad = 0;
+    const uint64_t end = elem_base + n;
+    for (uint32_t k = 0; k < n_tensors; ++k) {
+        uint64_t glo = tensor_offsets[k], ghi = tensor_offsets[k + 1];
+        if (ghi <= elem_base || glo >= end) continue;
+        if (glo < elem_base) glo = elem_base;
+        if (ghi > end) ghi = end;
+        const float wd = tensor_decay[k] ? cfg->decay_weight : cfg->no_decay_weight;
+        const int64_t lo = (int64_t)(glo - elem_base), hi = (int64_t)(ghi - elem_base);
+        int bad = 0;
+#pragma omp parallel for num_threads(threads) schedule(static) reduction(| : bad) if (hi - lo > 65536)
+        for (int64_t i = lo; i < hi; ++i) {
+            float gv = g_raw[i] / scale;
+            float gc = cfg->apply_clip ? gv * use_clip : gv;
+            float th, m1, v1;
+            bad |= adamw_core(master[i], gc, moment[i], variance[i], lr, wd, b1, b2, omb1, omb2,
+                              bc1, bc2, eps, &th, &m1, &v1);
+            master[i] = th;
+            moment[i] = m1;
+            variance[i] = v1;
+            bf16[i] = slmo_f32_to_bf16_bits(th);
+        }
+        any_bad |= bad;
+    }
+    return any_bad;
+}
+
 /* ---- the fused step ------------------------------------------------------------
  * unscale -> non-finite check -> fixed-tree norm -> clip -> AdamW per tensor
  * (decay weight by group, src/train/trainer.rs:274-293 with :276) -> bf16
@@ -440,30 +485,10 @@ int slmo_step(const slmo_step_config* cfg, const void* grads, int dtype, uint64_
         out->rejected = 1;
         out->status = SLMO_P12_OPTIMIZER_GRADIENT_INVALID;
     } else {
-        const float b1 = cfg->beta1, b2 = cfg->beta2, eps = cfg->epsilon;
-        const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
-        const float bc1 = 1.0f - slmo_powi(b1, (int32_t)cfg->one_based_update);
-        const float bc2 = 1.0f - slmo_powi(b2, (int32_t)cfg->one_based_update);
-        const float lr = cfg->learning_rate;
-        const float use_clip = cfg->apply_clip ? clip : 1.0f;
-        int any_bad = 0;
-        for (uint32_t k = 0; k < n_tensors; ++k) {
-            const float wd = tensor_decay[k] ? cfg->decay_weight : cfg->no_decay_weight;
-            const int64_t lo = (int64_t)tensor_offsets[k], hi = (int64_t)tensor_offsets[k + 1];
-            int bad = 0;
-#pragma omp parallel for num_threads(threads) schedule(static) reduction(| : bad) if (hi - lo > 65536)
-            for (int64_t i = lo; i < hi; ++i) {
-                float gc = cfg->apply_clip ? g[i] * use_clip : g[i];
-                float th, m1, v1;
-                bad |= adamw_core(master[i], gc, moment[i], variance[i], lr, wd, b1, b2, omb1,
-                                  omb2, bc1, bc2, eps, &th, &m1, &v1);
-                master[i] = th;
-                moment[i] = m1;
-                variance[i] = v1;
-                bf16[i] = slmo_f32_to_bf16_bits(th);
-            }
-            any_bad |= bad;
-        }
+        /* g is already unscaled: apply with scale 1 (x / 1 == x exactly). */
+        const int any_bad = slmo_adamw_apply_range(cfg, g, n, 0, tensor_offsets, tensor_decay,
+                                                   n_tensors, 1.0f, clip, master, moment,
+                                                   variance, bf16, threads);
         out->result_nonfinite = (uint32_t)any_bad;
         if (any_bad) out->status = SLMO_MODEL_OPTIMIZER_RESULT_NONFINITE;
         if (cfg->loss_scale_mode == SLMO_SCALE_DYNAMIC) {

@@ -130,6 +130,12 @@ typedef struct {
     uint32_t good_steps;
 } slmo_scaler;
 
+int slmo_adamw_apply_range(const slmo_step_config* cfg, const float* g_raw, uint64_t n,
+                           uint64_t elem_base, const uint64_t* tensor_offsets,
+                           const uint8_t* tensor_decay, uint32_t n_tensors, float scale,
+                           float clip, float* master, float* moment, float* variance,
+                           uint16_t* bf16, int threads);
+
 int slmo_step(const slmo_step_config* cfg, const void* grads, int dtype, uint64_t n,
               const uint64_t* tensor_offsets, const uint8_t* tensor_decay, uint32_t n_tensors,
               float* master, float* moment, float* variance, uint16_t* bf16,

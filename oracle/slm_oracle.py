@@ -114,6 +114,8 @@ def lib() -> ctypes.CDLL:
         "slmo_unscale_f32": (None, [P, U64, F, P, ctypes.c_int]),
         "slmo_unscale_bf16": (None, [P, U64, F, P, ctypes.c_int]),
         "slmo_rank_sum_bf16": (None, [P, U32, U64, P, ctypes.c_int]),
+        "slmo_adamw_apply_range": (ctypes.c_int, [ctypes.POINTER(StepConfig), P, U64, U64, P, P,
+                                                  U32, F, F, P, P, P, P, ctypes.c_int]),
         "slmo_step": (ctypes.c_int, [ctypes.POINTER(StepConfig), P, ctypes.c_int, U64, P, P, U32,
                                      P, P, P, P, ctypes.POINTER(Scaler),
                                      ctypes.POINTER(StepResult), ctypes.c_int]),
@@ -253,6 +255,19 @@ def step(cfg: StepConfig, grads: np.ndarray, offsets: np.ndarray, decay, state: 
                     ctypes.byref(scaler) if scaler is not None else None, ctypes.byref(res),
                     threads)
     return res
+
+
+def adamw_apply_range(cfg: StepConfig, g_raw: np.ndarray, elem_base: int, offsets, decay,
+                      scale: float, clip: float, state: dict, threads: int = 1) -> int:
+    """AdamW over a slice of the flat buffer (global start elem_base) with a
+    given clip; state holds the slice's master/moment/variance/bf16."""
+    g = np.ascontiguousarray(g_raw, dtype=np.float32)
+    off = np.ascontiguousarray(offsets, dtype=np.uint64)
+    dec = np.ascontiguousarray(np.asarray(decay, dtype=np.uint8))
+    return int(lib().slmo_adamw_apply_range(
+        ctypes.byref(cfg), _ptr(g), g.size, elem_base, _ptr(off), _ptr(dec), dec.size, scale, clip,
+        _ptr(state["master"]), _ptr(state["moment"]), _ptr(state["variance"]),
+        _ptr(state["bf16"]), threads))
 
 
 def apply_normalized_clipped_gradients(grads: np.ndarray, lr: float, t: int, offsets, decay,

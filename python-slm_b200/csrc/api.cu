@@ -1,38 +1,19 @@
 // C ABI of the optimizer step (include/slmopt.h): handle lifetime, state
 // codec, the fused step, the strict apply_update drop-in, the state hash.
-#include "../../include/slmopt.h"
+// The ZeRO-1 collectives live in zero1.cu.
+#include "handle.h"
 #include "sha256.h"
-#include "slmopt_internal.h"
-
-#include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cmath>
 #include <cstdio>
-#include <cstring>
 #include <new>
 #include <set>
-#include <string>
-#include <vector>
 
 using namespace slmopt;
 
-namespace {
+namespace slmopt {
 
 thread_local std::string g_last_error = "no error";
-
-int fail(int status, const std::string& msg) {
-  g_last_error = msg;
-  return status;
-}
-
-uint32_t f32_bits(float v) {
-  uint32_t b;
-  std::memcpy(&b, &v, 4);
-  return b;
-}
-
-bool finite_f32(float v) { return std::isfinite(v); }
 
 // Rust f32::powi with a run-time exponent: LLVM lowers it to the
 // compiler-builtins __powisf2 square-and-multiply loop (one f32 rounding per
@@ -51,64 +32,263 @@ float powi_f32(float base, int32_t exponent) {
   return recip ? 1.0f / product : product;
 }
 
-// Restores the caller's current device on scope exit.
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = false;
-  explicit DeviceGuard(int device) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    ok = cudaSetDevice(device) == cudaSuccess;
+AdamwParams adamw_params(const slm_step_config* cfg) {
+  AdamwParams p;
+  p.lr = cfg->learning_rate;
+  p.beta1 = cfg->beta1;
+  p.beta2 = cfg->beta2;
+  p.omb1 = 1.0f - cfg->beta1;
+  p.omb2 = 1.0f - cfg->beta2;
+  p.bc1 = 1.0f - powi_f32(cfg->beta1, int32_t(cfg->one_based_update));
+  p.bc2 = 1.0f - powi_f32(cfg->beta2, int32_t(cfg->one_based_update));
+  p.eps = cfg->epsilon;
+  p.decay_weight = cfg->decay_weight;
+  p.no_decay_weight = cfg->no_decay_weight;
+  return p;
+}
+
+int check_config(slm_opt_handle* h, const slm_step_config* cfg) {
+  if (!cfg) return h->err(SLM_ERR_INVALID_ARGUMENT, "cfg is NULL");
+  // src/model/oracle.rs:519-531: a zero update index or non-finite lr/decay.
+  if (cfg->one_based_update == 0 || cfg->one_based_update > 0x7fffffffu ||
+      !finite_f32(cfg->learning_rate) || !finite_f32(cfg->decay_weight) ||
+      !finite_f32(cfg->no_decay_weight))
+    return h->err(SLM_ERR_MODEL_OPTIMIZER_INPUT_INVALID,
+                  "OPT-001 requires finite state and a one-based update index");
+  if (!finite_f32(cfg->beta1) || !finite_f32(cfg->beta2) || !finite_f32(cfg->epsilon) ||
+      !(cfg->max_grad_norm > 0.0f) || !finite_f32(cfg->max_grad_norm) ||
+      !finite_f32(cfg->min_clip_accept))
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "non-finite or non-positive hyperparameter");
+  if (cfg->nonfinite_policy != SLM_NONFINITE_SKIP && cfg->nonfinite_policy != SLM_NONFINITE_ERROR)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown non-finite policy");
+  if (cfg->loss_scale_mode == SLM_SCALE_STATIC) {
+    if (!(cfg->static_loss_scale > 0.0f) || !finite_f32(cfg->static_loss_scale))
+      return h->err(SLM_ERR_INVALID_ARGUMENT, "the static loss scale must be positive and finite");
+  } else if (cfg->loss_scale_mode == SLM_SCALE_DYNAMIC) {
+    if (cfg->growth_interval == 0)
+      return h->err(SLM_ERR_INVALID_ARGUMENT, "the growth interval must be at least 1");
+  } else {
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown loss-scale mode");
   }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
+  return SLM_OK;
+}
+
+FinalizeParams finalize_params(const slm_opt_handle* h, const slm_step_config* cfg) {
+  FinalizeParams fp;
+  fp.max_grad_norm = cfg->max_grad_norm;
+  fp.min_clip_accept = cfg->min_clip_accept;
+  fp.apply_clip = cfg->apply_clip ? 1 : 0;
+  fp.nonfinite_policy = cfg->nonfinite_policy;
+  fp.dynamic = cfg->loss_scale_mode == SLM_SCALE_DYNAMIC ? 1 : 0;
+  fp.growth_interval = cfg->growth_interval;
+  fp.static_scale = cfg->static_loss_scale;
+  fp.total_chunks = h->sharded() ? uint32_t(h->world) * h->chunks_per_rank : h->n_chunks;
+  return fp;
+}
+
+void fill_result(const DeviceStepState& s, slm_step_result* out) {
+  out->sum_squares = s.sum_squares;
+  out->grad_norm = s.grad_norm;
+  out->clip_scale = s.clip_scale;
+  out->loss_scale_used = s.loss_scale_used;
+  out->next_loss_scale = s.next_loss_scale;
+  out->skipped = s.skipped;
+  out->nonfinite = s.nonfinite;
+  out->result_nonfinite = s.result_nonfinite;
+  out->rejected = s.rejected;
+  out->good_steps = s.good_steps;
+  out->status = s.status != 0 ? s.status
+                              : (s.result_nonfinite ? SLM_ERR_MODEL_OPTIMIZER_RESULT_NONFINITE
+                                                    : SLM_OK);
+}
+
+int read_state(slm_opt_handle* h, cudaStream_t s, DeviceStepState* out) {
+  int st = h->cuda(cudaMemcpyAsync(h->h_state, h->d_state, sizeof(DeviceStepState),
+                                   cudaMemcpyDeviceToHost, s),
+                   "result copy");
+  if (st) return st;
+  if (h->sharded()) {
+    if ((st = zero1_wait(h, s))) return st;
+  } else if ((st = h->cuda(cudaStreamSynchronize(s), "step sync"))) {
+    return st;
   }
-};
+  *out = *h->h_state;
+  return SLM_OK;
+}
+
+int allocate_state(slm_opt_handle* h, uint64_t w16_elems) {
+  const uint64_t L = h->shard_len;
+  const uint64_t chunks = (h->P + kChunkElems - 1) / kChunkElems;
+  if (chunks > 0xffffffffull)
+    return h->err(SLM_ERR_SIZE_LIMIT, "parameter count exceeds the chunk index range");
+  h->n_chunks = uint32_t(chunks);
+  const uint64_t tiles = (L + kTileElems - 1) / kTileElems;
+  std::vector<uint32_t> tile_first(tiles ? tiles : 1, 0);
+  {
+    uint32_t k = 0;
+    for (uint64_t t = 0; t < tiles; ++t) {
+      const uint64_t e = h->shard_begin + t * kTileElems;
+      while (e >= h->offsets[k + 1]) ++k;
+      tile_first[t] = k;
+    }
+  }
+  const uint64_t Ls = L ? L : 1;  // keep every pointer valid for an empty shard
+  int st;
+#define SLM_TRY(expr, what) \
+  if ((st = h->cuda((expr), what)) != SLM_OK) return st
+  SLM_TRY(cudaMalloc(&h->master, Ls * sizeof(float)), "cudaMalloc master");
+  SLM_TRY(cudaMalloc(&h->m1, Ls * sizeof(float)), "cudaMalloc m1");
+  SLM_TRY(cudaMalloc(&h->m2, Ls * sizeof(float)), "cudaMalloc m2");
+  SLM_TRY(cudaMalloc(&h->w16, w16_elems * sizeof(uint16_t)), "cudaMalloc bf16");
+  SLM_TRY(cudaMalloc(&h->d_offsets, h->offsets.size() * sizeof(uint64_t)), "cudaMalloc offsets");
+  SLM_TRY(cudaMalloc(&h->d_decay, h->decay.size()), "cudaMalloc decay");
+  SLM_TRY(cudaMalloc(&h->d_tile_first, tile_first.size() * sizeof(uint32_t)), "cudaMalloc tiles");
+  SLM_TRY(cudaMalloc(&h->d_partials, chunks * sizeof(double)), "cudaMalloc partials");
+  SLM_TRY(cudaMalloc(&h->d_state, sizeof(DeviceStepState)), "cudaMalloc state");
+  SLM_TRY(cudaMalloc(&h->d_scaler, sizeof(DeviceScaler)), "cudaMalloc scaler");
+  SLM_TRY(cudaMalloc(&h->d_flag, sizeof(uint32_t)), "cudaMalloc flag");
+  SLM_TRY(cudaMallocHost(&h->h_state, sizeof(DeviceStepState)), "cudaMallocHost state");
+  SLM_TRY(cudaMemset(h->master, 0, Ls * sizeof(float)), "memset master");
+  SLM_TRY(cudaMemset(h->m1, 0, Ls * sizeof(float)), "memset m1");
+  SLM_TRY(cudaMemset(h->m2, 0, Ls * sizeof(float)), "memset m2");
+  SLM_TRY(cudaMemset(h->w16, 0, w16_elems * sizeof(uint16_t)), "memset bf16");
+  SLM_TRY(cudaMemset(h->d_state, 0, sizeof(DeviceStepState)), "memset state");
+  SLM_TRY(cudaMemset(h->d_partials, 0, chunks * sizeof(double)), "memset partials");
+  SLM_TRY(cudaMemcpy(h->d_offsets, h->offsets.data(), h->offsets.size() * sizeof(uint64_t),
+                     cudaMemcpyHostToDevice),
+          "upload offsets");
+  SLM_TRY(cudaMemcpy(h->d_decay, h->decay.data(), h->decay.size(), cudaMemcpyHostToDevice),
+          "upload decay");
+  SLM_TRY(cudaMemcpy(h->d_tile_first, tile_first.data(), tile_first.size() * sizeof(uint32_t),
+                     cudaMemcpyHostToDevice),
+          "upload tile table");
+  const DeviceScaler sc{65536.0f, 0u};
+  SLM_TRY(cudaMemcpy(h->d_scaler, &sc, sizeof(sc), cudaMemcpyHostToDevice), "upload scaler");
+#undef SLM_TRY
+  h->grid_norm = norm_partials_grid(h->device);
+  h->grid_update[0] = adamw_update_grid(h->device, 0);
+  h->grid_update[1] = adamw_update_grid(h->device, 1);
+  return SLM_OK;
+}
+
+int build_table(slm_opt_handle* h, const slm_tensor_spec* table, uint32_t n_tensors) {
+  if (!table || n_tensors == 0)
+    return fail(SLM_ERR_P12_OPTIMIZER_STATE_INVALID, "the AdamW state contains no parameters");
+  std::set<std::string> seen;
+  h->offsets.assign(1, 0);
+  for (uint32_t k = 0; k < n_tensors; ++k) {
+    const char* name = table[k].name;
+    if (!name || !*name || table[k].elements == 0)
+      return fail(SLM_ERR_P12_OPTIMIZER_STATE_INVALID,
+                  "an AdamW parameter has an empty name or no elements");
+    if (!seen.insert(name).second)
+      return fail(SLM_ERR_P12_OPTIMIZER_PARAMETER_DUPLICATE,
+                  std::string("duplicate stable parameter name: ") + name);
+    h->names.emplace_back(name);
+    h->decay.push_back(table[k].weight_decay ? 1 : 0);
+    h->offsets.push_back(h->offsets.back() + table[k].elements);
+  }
+  h->P = h->offsets.back();
+  return SLM_OK;
+}
+
+}  // namespace slmopt
+
+namespace {
+
+int role_info(slm_opt_handle* h, int role, void** ptr, uint64_t* full_bytes,
+              uint64_t* shard_bytes) {
+  switch (role) {
+    case SLM_ROLE_PARAMETERS_BF16:
+      *ptr = h->w16;
+      *full_bytes = *shard_bytes = h->P * 2;
+      return SLM_OK;
+    case SLM_ROLE_MASTER_F32:
+      *ptr = h->master;
+      break;
+    case SLM_ROLE_MOMENT1_F32:
+      *ptr = h->m1;
+      break;
+    case SLM_ROLE_MOMENT2_F32:
+      *ptr = h->m2;
+      break;
+    default:
+      return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown artifact role");
+  }
+  *full_bytes = h->P * 4;
+  *shard_bytes = h->shard_len * 4;
+  return SLM_OK;
+}
+
+// Stage the gradient: device pointers are used in place (16-byte alignment
+// required for the vector loads), host pointers are copied into a staging
+// buffer on the step's stream.
+int stage_grads(slm_opt_handle* h, const void* grads, int dtype, int memory, cudaStream_t s,
+                const void** dev_grads) {
+  const size_t esize = dtype == SLM_DTYPE_F32 ? 4 : 2;
+  const size_t bytes = h->P * esize;
+  if (memory == SLM_MEMORY_DEVICE) {
+    if (reinterpret_cast<uintptr_t>(grads) % 16 != 0)
+      return h->err(SLM_ERR_INVALID_ARGUMENT, "device gradients must be 16-byte aligned");
+    *dev_grads = grads;
+    return SLM_OK;
+  }
+  if (memory != SLM_MEMORY_HOST) return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown memory kind");
+  if (h->staging_bytes < bytes) {
+    cudaFree(h->d_staging);
+    h->d_staging = nullptr;
+    h->staging_bytes = 0;
+    int st = h->cuda(cudaMalloc(&h->d_staging, bytes), "cudaMalloc gradient staging");
+    if (st) return st;
+    h->staging_bytes = bytes;
+  }
+  int st = h->cuda(cudaMemcpyAsync(h->d_staging, grads, bytes, cudaMemcpyHostToDevice, s),
+                   "gradient upload");
+  if (st) return st;
+  *dev_grads = h->d_staging;
+  return SLM_OK;
+}
+
+int enqueue_norm(slm_opt_handle* h, const void* dev_grads, int dtype, const slm_step_config* cfg,
+                 cudaStream_t s) {
+  const FinalizeParams fp = finalize_params(h, cfg);
+  return h->cuda(launch_norm_partials(dtype, dev_grads, h->P, 0, h->n_chunks, h->d_scaler,
+                                      h->d_partials, h->d_state, fp, h->grid_norm, s),
+                 "norm kernel");
+}
+
+int enqueue_update(slm_opt_handle* h, const void* dev_grads, int dtype,
+                   const slm_step_config* cfg, cudaStream_t s) {
+  const AdamwParams p = adamw_params(cfg);
+  return h->cuda(launch_adamw_update(dtype, dev_grads, h->P, 0, h->master, h->m1, h->m2, h->w16,
+                                     h->d_offsets, h->d_decay, h->d_tile_first, p, h->d_state,
+                                     h->grid_update[dtype == SLM_DTYPE_F32 ? 0 : 1], s),
+                 "update kernel");
+}
+
+int finish_result(slm_opt_handle* h, const DeviceStepState& ds, slm_step_result* out) {
+  fill_result(ds, out);
+  if (out->status != SLM_OK)
+    return h->err(out->status, std::string("optimizer step failed: ") +
+                                   slm_status_code_string(out->status));
+  return SLM_OK;
+}
+
+// Full host copy of one role (gathered across ranks for a ZeRO-1 handle).
+int download_role(slm_opt_handle* h, int role, void* dst, uint64_t bytes) {
+  void* ptr = nullptr;
+  uint64_t full = 0, shard = 0;
+  int st = role_info(h, role, &ptr, &full, &shard);
+  if (st) return st;
+  if (bytes != full)
+    return h->err(SLM_ERR_E1_STATE_ARTIFACT_INVALID,
+                  "a checkpoint artifact does not cover the exact parameter layout");
+  if (h->sharded() && role != SLM_ROLE_PARAMETERS_BF16)
+    return zero1_gather(h, ptr, 4, dst, nullptr);
+  return h->cuda(cudaMemcpy(dst, ptr, bytes, cudaMemcpyDeviceToHost), "snapshot copy");
+}
 
 }  // namespace
-
-struct slm_opt_handle {
-  int device = 0;
-  uint64_t P = 0;  // global parameter count
-  std::vector<std::string> names;
-  std::vector<uint64_t> offsets;  // n_tensors + 1 global offsets
-  std::vector<uint8_t> decay;
-  uint64_t shard_begin = 0, shard_len = 0;
-
-  float* master = nullptr;
-  float* m1 = nullptr;
-  float* m2 = nullptr;
-  uint16_t* w16 = nullptr;
-  uint64_t* d_offsets = nullptr;
-  uint8_t* d_decay = nullptr;
-  uint32_t* d_tile_first = nullptr;
-  double* d_partials = nullptr;
-  uint32_t n_chunks = 0;
-  DeviceStepState* d_state = nullptr;
-  DeviceScaler* d_scaler = nullptr;
-  uint32_t* d_flag = nullptr;
-  void* d_staging = nullptr;
-  size_t staging_bytes = 0;
-  DeviceStepState* h_state = nullptr;  // pinned
-
-  int grid_norm = 0;
-  int grid_update[2] = {0, 0};
-  // Gradients seen by the last norm pass (consumed by the update pass).
-  const void* pass_grads = nullptr;
-  int pass_dtype = -1;
-  cudaStream_t pending_stream = nullptr;
-  bool pending = false;
-  std::string last_error = "no error";
-
-  int err(int status, const std::string& msg) {
-    last_error = msg;
-    return fail(status, msg);
-  }
-  int cuda(cudaError_t e, const char* what) {
-    if (e == cudaSuccess) return SLM_OK;
-    const int st = (e == cudaErrorMemoryAllocation) ? SLM_ERR_OUT_OF_MEMORY : SLM_ERR_CUDA;
-    return err(st, std::string(what) + ": " + cudaGetErrorString(e));
-  }
-};
 
 extern "C" {
 
@@ -198,103 +378,34 @@ int slm_opt_create(const slm_tensor_spec* table, uint32_t n_tensors, int device,
                    slm_opt_handle** out) {
   if (!out) return fail(SLM_ERR_INVALID_ARGUMENT, "out is NULL");
   *out = nullptr;
-  if (!table || n_tensors == 0)
-    return fail(SLM_ERR_P12_OPTIMIZER_STATE_INVALID, "the AdamW state contains no parameters");
-  int count = 0;
-  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
-    return fail(SLM_ERR_NO_DEVICE, "no CUDA device is visible");
-  if (device < 0 || device >= count)
-    return fail(SLM_ERR_INVALID_ARGUMENT, "device ordinal out of range");
-
   slm_opt_handle* h = new (std::nothrow) slm_opt_handle();
   if (!h) return fail(SLM_ERR_OUT_OF_MEMORY, "host allocation failed");
-  h->device = device;
-  std::set<std::string> seen;
-  h->offsets.push_back(0);
-  for (uint32_t k = 0; k < n_tensors; ++k) {
-    const char* name = table[k].name;
-    if (!name || !*name || table[k].elements == 0) {
-      delete h;
-      return fail(SLM_ERR_P12_OPTIMIZER_STATE_INVALID,
-                  "an AdamW parameter has an empty name or no elements");
-    }
-    if (!seen.insert(name).second) {
-      delete h;
-      return fail(SLM_ERR_P12_OPTIMIZER_PARAMETER_DUPLICATE,
-                  std::string("duplicate stable parameter name: ") + name);
-    }
-    h->names.emplace_back(name);
-    h->decay.push_back(table[k].weight_decay ? 1 : 0);
-    h->offsets.push_back(h->offsets.back() + table[k].elements);
+  int st = build_table(h, table, n_tensors);
+  if (st) {
+    delete h;
+    return st;
   }
-  h->P = h->offsets.back();
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    delete h;
+    return fail(SLM_ERR_NO_DEVICE, "no CUDA device is visible");
+  }
+  if (device < 0 || device >= count) {
+    delete h;
+    return fail(SLM_ERR_INVALID_ARGUMENT, "device ordinal out of range");
+  }
+  h->device = device;
   h->shard_begin = 0;
   h->shard_len = h->P;
-
   DeviceGuard guard(device);
   if (!guard.ok) {
     delete h;
     return fail(SLM_ERR_CUDA, "cudaSetDevice failed");
   }
-  const uint64_t P = h->P;
-  const uint64_t chunks = (P + kChunkElems - 1) / kChunkElems;
-  if (chunks > 0xffffffffull) {
-    delete h;
-    return fail(SLM_ERR_SIZE_LIMIT, "parameter count exceeds the chunk index range");
+  if ((st = allocate_state(h, h->P))) {
+    slm_opt_destroy(h);
+    return st;
   }
-  h->n_chunks = uint32_t(chunks);
-  const uint64_t tiles = (P + kTileElems - 1) / kTileElems;
-  std::vector<uint32_t> tile_first(tiles);
-  {
-    uint32_t k = 0;
-    for (uint64_t t = 0; t < tiles; ++t) {
-      const uint64_t e = t * kTileElems;
-      while (e >= h->offsets[k + 1]) ++k;
-      tile_first[t] = k;
-    }
-  }
-  int st = SLM_OK;
-  // h->cuda() records the message in g_last_error before the handle is freed.
-#define SLM_TRY(expr, what)     \
-  do {                          \
-    st = h->cuda((expr), what); \
-    if (st != SLM_OK) {         \
-      slm_opt_destroy(h);       \
-      return st;                \
-    }                           \
-  } while (0)
-  SLM_TRY(cudaMalloc(&h->master, P * sizeof(float)), "cudaMalloc master");
-  SLM_TRY(cudaMalloc(&h->m1, P * sizeof(float)), "cudaMalloc m1");
-  SLM_TRY(cudaMalloc(&h->m2, P * sizeof(float)), "cudaMalloc m2");
-  SLM_TRY(cudaMalloc(&h->w16, P * sizeof(uint16_t)), "cudaMalloc bf16");
-  SLM_TRY(cudaMalloc(&h->d_offsets, h->offsets.size() * sizeof(uint64_t)), "cudaMalloc offsets");
-  SLM_TRY(cudaMalloc(&h->d_decay, h->decay.size()), "cudaMalloc decay");
-  SLM_TRY(cudaMalloc(&h->d_tile_first, tiles * sizeof(uint32_t)), "cudaMalloc tiles");
-  SLM_TRY(cudaMalloc(&h->d_partials, chunks * sizeof(double)), "cudaMalloc partials");
-  SLM_TRY(cudaMalloc(&h->d_state, sizeof(DeviceStepState)), "cudaMalloc state");
-  SLM_TRY(cudaMalloc(&h->d_scaler, sizeof(DeviceScaler)), "cudaMalloc scaler");
-  SLM_TRY(cudaMalloc(&h->d_flag, sizeof(uint32_t)), "cudaMalloc flag");
-  SLM_TRY(cudaMallocHost(&h->h_state, sizeof(DeviceStepState)), "cudaMallocHost state");
-  SLM_TRY(cudaMemset(h->master, 0, P * sizeof(float)), "memset master");
-  SLM_TRY(cudaMemset(h->m1, 0, P * sizeof(float)), "memset m1");
-  SLM_TRY(cudaMemset(h->m2, 0, P * sizeof(float)), "memset m2");
-  SLM_TRY(cudaMemset(h->w16, 0, P * sizeof(uint16_t)), "memset bf16");
-  SLM_TRY(cudaMemset(h->d_state, 0, sizeof(DeviceStepState)), "memset state");
-  SLM_TRY(cudaMemset(h->d_partials, 0, chunks * sizeof(double)), "memset partials");
-  SLM_TRY(cudaMemcpy(h->d_offsets, h->offsets.data(), h->offsets.size() * sizeof(uint64_t),
-                     cudaMemcpyHostToDevice),
-          "upload offsets");
-  SLM_TRY(cudaMemcpy(h->d_decay, h->decay.data(), h->decay.size(), cudaMemcpyHostToDevice),
-          "upload decay");
-  SLM_TRY(cudaMemcpy(h->d_tile_first, tile_first.data(), tiles * sizeof(uint32_t),
-                     cudaMemcpyHostToDevice),
-          "upload tile table");
-  const DeviceScaler sc{65536.0f, 0u};
-  SLM_TRY(cudaMemcpy(h->d_scaler, &sc, sizeof(sc), cudaMemcpyHostToDevice), "upload scaler");
-#undef SLM_TRY
-  h->grid_norm = norm_partials_grid(device);
-  h->grid_update[0] = adamw_update_grid(device, 0);
-  h->grid_update[1] = adamw_update_grid(device, 1);
   *out = h;
   return SLM_OK;
 }
@@ -302,6 +413,7 @@ int slm_opt_create(const slm_tensor_spec* table, uint32_t n_tensors, int device,
 int slm_opt_destroy(slm_opt_handle* h) {
   if (!h) return SLM_OK;
   DeviceGuard guard(h->device);
+  zero1_release(h);
   cudaFree(h->master);
   cudaFree(h->m1);
   cudaFree(h->m2);
@@ -325,33 +437,10 @@ const char* slm_opt_last_error(const slm_opt_handle* h) {
   return h ? h->last_error.c_str() : g_last_error.c_str();
 }
 
-static int role_buffer(slm_opt_handle* h, int role, void** ptr, uint64_t* bytes) {
-  switch (role) {
-    case SLM_ROLE_PARAMETERS_BF16:
-      *ptr = h->w16;
-      *bytes = h->P * 2;
-      return SLM_OK;
-    case SLM_ROLE_MASTER_F32:
-      *ptr = h->master;
-      *bytes = h->shard_len * 4;
-      return SLM_OK;
-    case SLM_ROLE_MOMENT1_F32:
-      *ptr = h->m1;
-      *bytes = h->shard_len * 4;
-      return SLM_OK;
-    case SLM_ROLE_MOMENT2_F32:
-      *ptr = h->m2;
-      *bytes = h->shard_len * 4;
-      return SLM_OK;
-    default:
-      return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown artifact role");
-  }
-}
-
 int slm_opt_device_buffer(slm_opt_handle* h, int role, void** out_device_ptr) {
   if (!h || !out_device_ptr) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
-  uint64_t bytes = 0;
-  return role_buffer(h, role, out_device_ptr, &bytes);
+  uint64_t full = 0, shard = 0;
+  return role_info(h, role, out_device_ptr, &full, &shard);
 }
 
 int slm_opt_init_master(slm_opt_handle* h, const float* master_host, void* stream) {
@@ -362,37 +451,44 @@ int slm_opt_init_master(slm_opt_handle* h, const float* master_host, void* strea
                                    h->shard_len * sizeof(float), cudaMemcpyHostToDevice, s),
                    "upload master");
   if (st) return st;
-  st = h->cuda(launch_init_from_master(h->master, h->m1, h->m2, h->w16 + h->shard_begin,
-                                       h->shard_len, s),
-               "init kernel");
-  if (st) return st;
-  return h->cuda(cudaStreamSynchronize(s), "init sync");
+  if (h->shard_len) {
+    st = h->cuda(launch_init_from_master(h->master, h->m1, h->m2, h->w16 + h->shard_begin,
+                                         h->shard_len, s),
+                 "init kernel");
+    if (st) return st;
+  }
+  if ((st = h->cuda(cudaStreamSynchronize(s), "init sync"))) return st;
+  if (h->sharded())  // every rank needs every shard's bf16 weights
+    return zero1_gather(h, h->w16 + h->shard_begin, 2, nullptr, s);
+  return SLM_OK;
 }
 
 int slm_opt_snapshot(slm_opt_handle* h, int role, void* host_dst, uint64_t bytes) {
   if (!h || !host_dst) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
   void* ptr = nullptr;
-  uint64_t want = 0;
-  int st = role_buffer(h, role, &ptr, &want);
+  uint64_t full = 0, shard = 0;
+  int st = role_info(h, role, &ptr, &full, &shard);
   if (st) return st;
-  if (bytes != want)
-    return h->err(SLM_ERR_E1_STATE_ARTIFACT_INVALID,
-                  "a checkpoint artifact does not cover the exact parameter layout");
   DeviceGuard guard(h->device);
-  return h->cuda(cudaMemcpy(host_dst, ptr, bytes, cudaMemcpyDeviceToHost), "snapshot copy");
+  if (h->sharded() && bytes == shard && bytes != full)
+    return h->cuda(cudaMemcpy(host_dst, ptr, bytes, cudaMemcpyDeviceToHost), "shard copy");
+  return download_role(h, role, host_dst, bytes);
 }
 
 int slm_opt_restore(slm_opt_handle* h, int role, const void* host_src, uint64_t bytes) {
   if (!h || !host_src) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
   void* ptr = nullptr;
-  uint64_t want = 0;
-  int st = role_buffer(h, role, &ptr, &want);
+  uint64_t full = 0, shard = 0;
+  int st = role_info(h, role, &ptr, &full, &shard);
   if (st) return st;
-  if (bytes != want)
+  if (bytes != full)
     return h->err(SLM_ERR_E1_STATE_ARTIFACT_INVALID,
                   "a checkpoint artifact does not cover the exact parameter layout");
   DeviceGuard guard(h->device);
-  return h->cuda(cudaMemcpy(ptr, host_src, bytes, cudaMemcpyHostToDevice), "restore copy");
+  if (role == SLM_ROLE_PARAMETERS_BF16)
+    return h->cuda(cudaMemcpy(ptr, host_src, bytes, cudaMemcpyHostToDevice), "restore copy");
+  const uint8_t* src = static_cast<const uint8_t*>(host_src) + h->shard_begin * 4;
+  return h->cuda(cudaMemcpy(ptr, src, shard, cudaMemcpyHostToDevice), "restore copy");
 }
 
 int slm_opt_validate_state(slm_opt_handle* h) {
@@ -400,10 +496,12 @@ int slm_opt_validate_state(slm_opt_handle* h) {
   DeviceGuard guard(h->device);
   int st = h->cuda(cudaMemset(h->d_flag, 0, sizeof(uint32_t)), "validate memset");
   if (st) return st;
-  st = h->cuda(launch_validate_state(h->master, h->m1, h->m2, h->w16 + h->shard_begin,
-                                     h->shard_len, h->d_flag, nullptr),
-               "validate kernel");
-  if (st) return st;
+  if (h->shard_len) {
+    st = h->cuda(launch_validate_state(h->master, h->m1, h->m2, h->w16 + h->shard_begin,
+                                       h->shard_len, h->d_flag, nullptr),
+                 "validate kernel");
+    if (st) return st;
+  }
   uint32_t bad = 0;
   st = h->cuda(cudaMemcpy(&bad, h->d_flag, sizeof(bad), cudaMemcpyDeviceToHost), "validate read");
   if (st) return st;
@@ -433,167 +531,6 @@ int slm_opt_get_loss_scale(slm_opt_handle* h, float* scale, uint32_t* good_steps
   return SLM_OK;
 }
 
-}  // extern "C"
-
-namespace {
-
-int check_config(slm_opt_handle* h, const slm_step_config* cfg) {
-  if (!cfg) return h->err(SLM_ERR_INVALID_ARGUMENT, "cfg is NULL");
-  // src/model/oracle.rs:519-531: a zero update index or non-finite lr/decay.
-  if (cfg->one_based_update == 0 || cfg->one_based_update > 0x7fffffffu ||
-      !finite_f32(cfg->learning_rate) || !finite_f32(cfg->decay_weight) ||
-      !finite_f32(cfg->no_decay_weight))
-    return h->err(SLM_ERR_MODEL_OPTIMIZER_INPUT_INVALID,
-                  "OPT-001 requires finite state and a one-based update index");
-  if (!finite_f32(cfg->beta1) || !finite_f32(cfg->beta2) || !finite_f32(cfg->epsilon) ||
-      !(cfg->max_grad_norm > 0.0f) || !finite_f32(cfg->max_grad_norm) ||
-      !finite_f32(cfg->min_clip_accept))
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "non-finite or non-positive hyperparameter");
-  if (cfg->nonfinite_policy != SLM_NONFINITE_SKIP && cfg->nonfinite_policy != SLM_NONFINITE_ERROR)
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown non-finite policy");
-  if (cfg->loss_scale_mode == SLM_SCALE_STATIC) {
-    if (!(cfg->static_loss_scale > 0.0f) || !finite_f32(cfg->static_loss_scale))
-      return h->err(SLM_ERR_INVALID_ARGUMENT, "the static loss scale must be positive and finite");
-  } else if (cfg->loss_scale_mode == SLM_SCALE_DYNAMIC) {
-    if (cfg->growth_interval == 0)
-      return h->err(SLM_ERR_INVALID_ARGUMENT, "the growth interval must be at least 1");
-  } else {
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown loss-scale mode");
-  }
-  return SLM_OK;
-}
-
-AdamwParams adamw_params(const slm_step_config* cfg) {
-  AdamwParams p;
-  p.lr = cfg->learning_rate;
-  p.beta1 = cfg->beta1;
-  p.beta2 = cfg->beta2;
-  p.omb1 = 1.0f - cfg->beta1;
-  p.omb2 = 1.0f - cfg->beta2;
-  p.bc1 = 1.0f - powi_f32(cfg->beta1, int32_t(cfg->one_based_update));
-  p.bc2 = 1.0f - powi_f32(cfg->beta2, int32_t(cfg->one_based_update));
-  p.eps = cfg->epsilon;
-  p.decay_weight = cfg->decay_weight;
-  p.no_decay_weight = cfg->no_decay_weight;
-  return p;
-}
-
-FinalizeParams finalize_params(const slm_opt_handle* h, const slm_step_config* cfg) {
-  FinalizeParams fp;
-  fp.max_grad_norm = cfg->max_grad_norm;
-  fp.min_clip_accept = cfg->min_clip_accept;
-  fp.apply_clip = cfg->apply_clip ? 1 : 0;
-  fp.nonfinite_policy = cfg->nonfinite_policy;
-  fp.dynamic = cfg->loss_scale_mode == SLM_SCALE_DYNAMIC ? 1 : 0;
-  fp.growth_interval = cfg->growth_interval;
-  fp.static_scale = cfg->static_loss_scale;
-  fp.total_chunks = h->n_chunks;
-  return fp;
-}
-
-void fill_result(const DeviceStepState& s, slm_step_result* out) {
-  out->sum_squares = s.sum_squares;
-  out->grad_norm = s.grad_norm;
-  out->clip_scale = s.clip_scale;
-  out->loss_scale_used = s.loss_scale_used;
-  out->next_loss_scale = s.next_loss_scale;
-  out->skipped = s.skipped;
-  out->nonfinite = s.nonfinite;
-  out->result_nonfinite = s.result_nonfinite;
-  out->rejected = s.rejected;
-  out->good_steps = s.good_steps;
-  out->status = s.status != 0 ? s.status
-                              : (s.result_nonfinite ? SLM_ERR_MODEL_OPTIMIZER_RESULT_NONFINITE
-                                                    : SLM_OK);
-}
-
-// Stage the gradient: device pointers are used in place (16-byte alignment
-// required for the vector loads), host pointers are copied into a staging
-// buffer on the step's stream.
-int stage_grads(slm_opt_handle* h, const void* grads, int dtype, int memory, cudaStream_t s,
-                const void** dev_grads) {
-  const size_t esize = dtype == SLM_DTYPE_F32 ? 4 : 2;
-  const size_t bytes = h->P * esize;
-  if (memory == SLM_MEMORY_DEVICE) {
-    if (reinterpret_cast<uintptr_t>(grads) % 16 != 0)
-      return h->err(SLM_ERR_INVALID_ARGUMENT, "device gradients must be 16-byte aligned");
-    *dev_grads = grads;
-    return SLM_OK;
-  }
-  if (memory != SLM_MEMORY_HOST) return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown memory kind");
-  if (h->staging_bytes < bytes) {
-    cudaFree(h->d_staging);
-    h->d_staging = nullptr;
-    h->staging_bytes = 0;
-    int st = h->cuda(cudaMalloc(&h->d_staging, bytes), "cudaMalloc gradient staging");
-    if (st) return st;
-    h->staging_bytes = bytes;
-  }
-  int st = h->cuda(cudaMemcpyAsync(h->d_staging, grads, bytes, cudaMemcpyHostToDevice, s),
-                   "gradient upload");
-  if (st) return st;
-  *dev_grads = h->d_staging;
-  return SLM_OK;
-}
-
-int enqueue_norm(slm_opt_handle* h, const void* dev_grads, int dtype, const slm_step_config* cfg,
-                 cudaStream_t s) {
-  const FinalizeParams fp = finalize_params(h, cfg);
-  return h->cuda(launch_norm_partials(dtype, dev_grads, h->P, 0, h->n_chunks, h->d_scaler,
-                                      h->d_partials, h->d_state, fp, h->grid_norm, s),
-                 "norm kernel");
-}
-
-int enqueue_update(slm_opt_handle* h, const void* dev_grads, int dtype,
-                   const slm_step_config* cfg, cudaStream_t s) {
-  const AdamwParams p = adamw_params(cfg);
-  return h->cuda(launch_adamw_update(dtype, dev_grads, h->P, 0, h->master, h->m1, h->m2, h->w16,
-                                     h->d_offsets, h->d_decay, h->d_tile_first, p, h->d_state,
-                                     h->grid_update[dtype == SLM_DTYPE_F32 ? 0 : 1], s),
-                 "update kernel");
-}
-
-int read_state(slm_opt_handle* h, cudaStream_t s, DeviceStepState* out) {
-  int st = h->cuda(cudaMemcpyAsync(h->h_state, h->d_state, sizeof(DeviceStepState),
-                                   cudaMemcpyDeviceToHost, s),
-                   "result copy");
-  if (st) return st;
-  st = h->cuda(cudaStreamSynchronize(s), "step sync");
-  if (st) return st;
-  *out = *h->h_state;
-  return SLM_OK;
-}
-
-}  // namespace
-
-extern "C" {
-
-int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
-                 const slm_step_config* cfg, slm_step_result* out, void* stream) {
-  if (!h || !grads) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
-  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
-  int st = check_config(h, cfg);
-  if (st) return st;
-  DeviceGuard guard(h->device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const void* dev = nullptr;
-  if ((st = stage_grads(h, grads, dtype, memory, s, &dev))) return st;
-  if ((st = enqueue_norm(h, dev, dtype, cfg, s))) return st;
-  if ((st = enqueue_update(h, dev, dtype, cfg, s))) return st;
-  h->pending = true;
-  h->pending_stream = s;
-  if (!out) return SLM_OK;
-  DeviceStepState ds;
-  if ((st = read_state(h, s, &ds))) return st;
-  h->pending = false;
-  fill_result(ds, out);
-  if (out->status != SLM_OK)
-    return h->err(out->status, std::string("optimizer step failed: ") +
-                                   slm_status_code_string(out->status));
-  return SLM_OK;
-}
-
 int slm_opt_norm_pass(slm_opt_handle* h, const void* grads, int dtype, int memory,
                       const slm_step_config* cfg, void* stream) {
   if (!h || !grads) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
@@ -601,6 +538,8 @@ int slm_opt_norm_pass(slm_opt_handle* h, const void* grads, int dtype, int memor
     return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
   int st = check_config(h, cfg);
   if (st) return st;
+  if (h->sharded())
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "a ZeRO-1 handle runs whole steps (slm_opt_step)");
   DeviceGuard guard(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const void* dev = nullptr;
@@ -629,6 +568,34 @@ int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* str
   return st;
 }
 
+int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
+                 const slm_step_config* cfg, slm_step_result* out, void* stream) {
+  if (!h || !grads) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  int st = check_config(h, cfg);
+  if (st) return st;
+  if (h->broken)
+    return h->err(SLM_ERR_TIMEOUT, "a previous collective timed out; the communicator is closed");
+  DeviceGuard guard(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (h->sharded()) {
+    if ((st = zero1_step(h, grads, dtype, memory, cfg, s))) return st;
+  } else {
+    const void* dev = nullptr;
+    if ((st = stage_grads(h, grads, dtype, memory, s, &dev))) return st;
+    if ((st = enqueue_norm(h, dev, dtype, cfg, s))) return st;
+    if ((st = enqueue_update(h, dev, dtype, cfg, s))) return st;
+  }
+  h->pending = true;
+  h->pending_stream = s;
+  if (!out) return SLM_OK;
+  DeviceStepState ds;
+  if ((st = read_state(h, s, &ds))) return st;
+  h->pending = false;
+  return finish_result(h, ds, out);
+}
+
 int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out) {
   if (!h || !out) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
   DeviceGuard guard(h->device);
@@ -636,11 +603,7 @@ int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out) {
   int st = read_state(h, h->pending ? h->pending_stream : nullptr, &ds);
   if (st) return st;
   h->pending = false;
-  fill_result(ds, out);
-  if (out->status != SLM_OK)
-    return h->err(out->status, std::string("optimizer step failed: ") +
-                                   slm_status_code_string(out->status));
-  return SLM_OK;
+  return finish_result(h, ds, out);
 }
 
 int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
@@ -648,6 +611,9 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
                          uint64_t valid_targets, char* out_sha256_hex65) {
   (void)valid_targets;  // unused by the reference's CUDA backend (cuda_backend.rs:245)
   if (!h || !grads_host) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (h->sharded())
+    return h->err(SLM_ERR_INVALID_ARGUMENT,
+                  "apply_update is the single-replica drop-in; use slm_opt_step for ZeRO-1");
   // trainer.rs:235-249: one FP32 gradient per parameter.
   if (n != h->P) {
     char msg[192];
@@ -660,16 +626,15 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   }
   slm_step_config cfg;
   slm_step_config_default(&cfg);
-  cfg.learning_rate = learning_rate;
+  cfg.learning_rate = finite_f32(learning_rate) ? learning_rate : 0.0f;
   cfg.one_based_update = one_based_update >= 1 && one_based_update <= 0x7fffffffu
                              ? uint32_t(one_based_update)
                              : 1u;
-  cfg.apply_clip = 0;              // the input is already clipped
+  cfg.apply_clip = 0;                  // the input is already clipped
   cfg.min_clip_accept = 1.0f - 0.05f;  // CLIP_VERIFICATION_TOLERANCE, trainer.rs:161
   cfg.nonfinite_policy = SLM_NONFINITE_ERROR;
   cfg.loss_scale_mode = SLM_SCALE_STATIC;
   cfg.static_loss_scale = 1.0f;
-  if (!finite_f32(learning_rate)) cfg.learning_rate = 0.0f;  // reported below in order
 
   DeviceGuard guard(h->device);
   cudaStream_t s = nullptr;
@@ -713,20 +678,24 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
 
 int slm_opt_state_sha256(slm_opt_handle* h, char out_hex[65]) {
   if (!h || !out_hex) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
-  if (h->shard_len != h->P)
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "the state hash needs the full (gathered) state");
   int st = slm_opt_validate_state(h);
   if (st) return st;
   DeviceGuard guard(h->device);
+  // Full host copies (gathered for a ZeRO-1 handle: collective).
+  std::vector<float> master(h->P), m1(h->P), m2(h->P);
+  std::vector<uint16_t> w16(h->P);
+  if ((st = download_role(h, SLM_ROLE_MASTER_F32, master.data(), h->P * 4))) return st;
+  if ((st = download_role(h, SLM_ROLE_MOMENT1_F32, m1.data(), h->P * 4))) return st;
+  if ((st = download_role(h, SLM_ROLE_MOMENT2_F32, m2.data(), h->P * 4))) return st;
+  if ((st = download_role(h, SLM_ROLE_PARAMETERS_BF16, w16.data(), h->P * 2))) return st;
   // trainer.rs:297-320: tag (with NUL), then per tensor: name length (u64 LE),
-  // name, decay byte, element count (u64 LE), master, bf16, m, v (LE bytes).
+  // name, decay byte, element count (u64 LE), master, bf16, m, v (LE bytes;
+  // x86-64 and the device are little-endian, so the arrays hash as stored).
   Sha256 sha;
   static const char tag[] = "python-slm/adamw-state/v1";
   sha.update(tag, sizeof(tag));
-  const size_t block_elems = size_t(1) << 24;  // 64 MB of f32 per copy
-  std::vector<uint8_t> buf;
   for (size_t k = 0; k < h->names.size(); ++k) {
-    const uint64_t lo = h->offsets[k], hi = h->offsets[k + 1], count = hi - lo;
+    const uint64_t lo = h->offsets[k], count = h->offsets[k + 1] - lo;
     uint8_t le[8];
     const uint64_t name_len = h->names[k].size();
     for (int b = 0; b < 8; ++b) le[b] = uint8_t(name_len >> (8 * b));
@@ -736,19 +705,10 @@ int slm_opt_state_sha256(slm_opt_handle* h, char out_hex[65]) {
     sha.update(&d, 1);
     for (int b = 0; b < 8; ++b) le[b] = uint8_t(count >> (8 * b));
     sha.update(le, 8);
-    const void* arrays[4] = {h->master, h->w16, h->m1, h->m2};
-    const size_t sizes[4] = {4, 2, 4, 4};
-    for (int a = 0; a < 4; ++a) {
-      for (uint64_t at = lo; at < hi; at += block_elems) {
-        const uint64_t len = std::min<uint64_t>(block_elems, hi - at);
-        buf.resize(len * sizes[a]);
-        const uint8_t* src = static_cast<const uint8_t*>(arrays[a]) + at * sizes[a];
-        if ((st = h->cuda(cudaMemcpy(buf.data(), src, len * sizes[a], cudaMemcpyDeviceToHost),
-                          "hash download")))
-          return st;
-        sha.update(buf.data(), buf.size());
-      }
-    }
+    sha.update(master.data() + lo, count * 4);
+    sha.update(w16.data() + lo, count * 2);
+    sha.update(m1.data() + lo, count * 4);
+    sha.update(m2.data() + lo, count * 4);
   }
   uint8_t digest[32];
   sha.final(digest);

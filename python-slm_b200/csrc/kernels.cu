@@ -126,37 +126,84 @@ __device__ __forceinline__ double block_fold(double v, double* warp_sums) {
   return r;
 }
 
+__device__ __forceinline__ void load_full8(const float* __restrict__ g, float (&x)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(g));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(g + 4));
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ void load_full8(const uint16_t* __restrict__ g, float (&x)[8]) {
+  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(g)), x);
+}
+
 template <typename GT, bool kMul>
 __device__ __forceinline__ double chunk_thread_sum(const GT* __restrict__ g, uint64_t base,
                                                    uint64_t n, const ScaleInfo& sc) {
   double acc = 0.0;
-#pragma unroll 8
+  if (base + kChunkElems <= n) {
+    // Whole chunk in range: kNormBatch unguarded loads go out together, then
+    // their squares are added in the tree's element order.
+    const GT* p = g + base + static_cast<uint64_t>(threadIdx.x) * kVec;
+#pragma unroll 1
+    for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kNormBatch) {
+      float x[kNormBatch][kVec];
+#pragma unroll
+      for (uint32_t b = 0; b < kNormBatch; ++b)
+        load_full8(p + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec), x[b]);
+#pragma unroll
+      for (uint32_t b = 0; b < kNormBatch; ++b) {
+#pragma unroll
+        for (uint32_t j = 0; j < kVec; ++j) {
+          const double d = static_cast<double>(unscale<kMul>(x[b][j], sc));
+          // d*d is exact in f64 (24-bit significands), so the FMA rounds
+          // once, exactly like acc + d*d.
+          acc = __fma_rn(d, d, acc);
+        }
+      }
+    }
+    return acc;
+  }
   for (uint32_t k = 0; k < kChunkIters; ++k) {
     const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
                         static_cast<uint64_t>(threadIdx.x) * kVec;
+    if (e0 >= n) break;  // the rest adds +0.0
     float x[kVec];
     load_grad8(g, e0, n, x);
 #pragma unroll
     for (uint32_t j = 0; j < kVec; ++j) {
       const double d = static_cast<double>(unscale<kMul>(x[j], sc));
-      // d*d is exact in f64 (24-bit significands), so the FMA rounds once,
-      // exactly like acc + d*d.
       acc = __fma_rn(d, d, acc);
     }
   }
   return acc;
 }
 
-// Last block: reduce the partials, decide clip / skip, advance the scaler.
-__device__ void finalize_block(const double* partials, DeviceStepState* st, DeviceScaler* scaler,
+// Chunk partials in global chunk order.  A single replica stores them densely;
+// a ZeRO-1 group all-gathers per-rank blocks of per_rank partials followed by
+// one flag slot, so chunk c lives at (c / per_rank) * stride + c % per_rank.
+struct PartialsView {
+  const double* p;
+  uint32_t per_rank;
+  uint32_t stride;
+  __device__ __forceinline__ double operator()(uint32_t c) const {
+    const uint32_t q = c / per_rank;
+    return __ldcg(p + static_cast<uint64_t>(q) * stride + (c - q * per_rank));
+  }
+};
+
+// Reduce the partials with the fixed tree, decide clip / skip, advance the
+// scaler.  Called by one whole 256-thread block; `nonfinite` is read from
+// thread 0 only.
+__device__ void finalize_block(const PartialsView& partials, uint32_t nonfinite,
+                               DeviceStepState* st, DeviceScaler* scaler,
                                const FinalizeParams& fp, double* warp_sums) {
   double v = 0.0;
   for (uint32_t c = threadIdx.x; c < fp.total_chunks; c += kTreeThreads)
-    v = __dadd_rn(v, __ldcg(partials + c));
+    v = __dadd_rn(v, partials(c));
   const double sum = block_fold(v, warp_sums);
   if (threadIdx.x != 0) return;
 
-  const uint32_t nonfinite = atomicExch(&st->nonfinite_accum, 0u) != 0u ? 1u : 0u;
   const float scale = fp.dynamic ? scaler->scale : fp.static_scale;
   const float sumf = __double2float_rn(sum);
   const bool norm_bad = !finite_f32(sumf);
@@ -240,7 +287,100 @@ __global__ void __launch_bounds__(kTreeThreads)
   __syncthreads();
   if (s_last == 0u) return;
   __threadfence();
-  finalize_block(partials, st, scaler, fp, warp_sums);
+  const uint32_t nonfinite =
+      threadIdx.x == 0 ? (atomicExch(&st->nonfinite_accum, 0u) != 0u ? 1u : 0u) : 0u;
+  finalize_block(PartialsView{partials, fp.total_chunks, fp.total_chunks}, nonfinite, st, scaler,
+                 fp, warp_sums);
+}
+
+// ---- ZeRO-1 -----------------------------------------------------------------------
+// After the all-to-all, recv holds `ranks` slices of this rank's shard (slice q
+// from rank q, `stride` elements apart).  One pass sums them in rank order
+// 0..N-1 in f32 (the reference's accumulation order, trainer.rs:865-877),
+// stores the raw sums for the update pass, and forms the chunk partials of the
+// unscaled sums with the same fixed tree as a single replica.  The last block
+// appends the non-finite flag as slot n_chunks of the send buffer.
+template <typename GT, bool kMul>
+__device__ __forceinline__ double zero1_thread_sum(const GT* __restrict__ recv, uint32_t ranks,
+                                                   uint64_t stride, uint64_t base, uint64_t n,
+                                                   float* __restrict__ gsum,
+                                                   const ScaleInfo& sc) {
+  double acc = 0.0;
+#pragma unroll 2
+  for (uint32_t k = 0; k < kChunkIters; ++k) {
+    const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
+                        static_cast<uint64_t>(threadIdx.x) * kVec;
+    if (e0 >= n) break;
+    float s[kVec];
+    load_grad8(recv, e0, n, s);
+    for (uint32_t q = 1; q < ranks; ++q) {
+      float x[kVec];
+      load_grad8(recv + static_cast<uint64_t>(q) * stride, e0, n, x);
+#pragma unroll
+      for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
+    }
+    if (e0 + kVec <= n) {
+      __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
+      __stcg(reinterpret_cast<float4*>(gsum + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
+    } else {
+      for (uint32_t j = 0; j < kVec && e0 + j < n; ++j) gsum[e0 + j] = s[j];
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+      const double d = static_cast<double>(unscale<kMul>(s[j], sc));
+      acc = __fma_rn(d, d, acc);
+    }
+  }
+  return acc;
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kTreeThreads)
+    zero1_reduce_kernel(const GT* __restrict__ recv, uint32_t ranks, uint64_t stride,
+                        uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
+                        FinalizeParams fp, float* __restrict__ gsum, double* __restrict__ send,
+                        DeviceStepState* st) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  __shared__ uint32_t s_last;
+  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
+  bool bad = false;
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
+    const double acc =
+        sc.mul ? zero1_thread_sum<GT, true>(recv, ranks, stride, base, n_valid, gsum, sc)
+               : zero1_thread_sum<GT, false>(recv, ranks, stride, base, n_valid, gsum, sc);
+    bad |= !isfinite(acc);
+    const double total = block_fold(acc, warp_sums);
+    if (threadIdx.x == 0) send[c] = total;
+  }
+  const int any_bad = __syncthreads_or(bad ? 1 : 0);
+  if (threadIdx.x == 0) {
+    if (any_bad) atomicOr(&st->nonfinite_accum, 1u);
+    __threadfence();
+    s_last = (atomicAdd(&st->blocks_done, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (s_last == 0u || threadIdx.x != 0) return;
+  __threadfence();
+  send[n_chunks] = atomicExch(&st->nonfinite_accum, 0u) != 0u ? 1.0 : 0.0;
+  st->blocks_done = 0u;
+  __threadfence();
+}
+
+// Every rank reduces the all-gathered partials of all ranks in global chunk
+// order, so the norm, clip and skip decision are bit-identical on all ranks
+// and equal to a single replica's.
+__global__ void __launch_bounds__(kTreeThreads)
+    zero1_finalize_kernel(const double* __restrict__ gathered, uint32_t ranks,
+                          uint32_t per_rank, DeviceScaler* scaler, DeviceStepState* st,
+                          FinalizeParams fp) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  uint32_t nonfinite = 0u;
+  if (threadIdx.x == 0)
+    for (uint32_t q = 0; q < ranks; ++q)
+      nonfinite |= gathered[static_cast<uint64_t>(q) * (per_rank + 1) + per_rank] != 0.0 ? 1u : 0u;
+  finalize_block(PartialsView{gathered, per_rank, per_rank + 1}, nonfinite, st, scaler, fp,
+                 warp_sums);
 }
 
 // ---- AdamW update -------------------------------------------------------------
@@ -284,6 +424,25 @@ __device__ __forceinline__ float ld_grad1(const uint16_t* __restrict__ g, uint64
   return __uint_as_float(static_cast<uint32_t>(g[i]) << 16);
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (no registers, no shared memory):
+// keeps the next tile's bytes in flight while this tile computes.  p and bytes
+// must be multiples of 16.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <typename GT>
+__device__ __forceinline__ void prefetch_tile(uint64_t tile, uint64_t n, const GT* g,
+                                              const float* master, const float* mom,
+                                              const float* var) {
+  const uint64_t e0 = tile * kTileElems;
+  if (e0 + kTileElems > n) return;  // only whole tiles (16-byte multiples)
+  prefetch_l2(g + e0, kTileElems * sizeof(GT));
+  prefetch_l2(master + e0, kTileElems * 4);
+  prefetch_l2(mom + e0, kTileElems * 4);
+  prefetch_l2(var + e0, kTileElems * 4);
+}
+
 // Decay weight of global element e, scanning forward from tensor k.
 __device__ __forceinline__ float decay_of(uint64_t e, uint32_t& k,
                                           const uint64_t* __restrict__ offsets,
@@ -305,7 +464,16 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
                                             float clip) {
   bool bad = false;
   const uint64_t n_tiles = (n + kTileElems - 1) / kTileElems;
+  if constexpr (kUpdatePrefetch > 0) {
+    if (threadIdx.x == 0)
+      for (uint32_t d = 1; d < kUpdatePrefetch; ++d)
+        prefetch_tile(blockIdx.x + uint64_t(d) * gridDim.x, n, g, master, mom, var);
+  }
   for (uint64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    if constexpr (kUpdatePrefetch > 0) {
+      if (threadIdx.x == 0)
+        prefetch_tile(tile + uint64_t(kUpdatePrefetch) * gridDim.x, n, g, master, mom, var);
+    }
     const uint32_t first = __ldg(tile_first + tile);
     uint64_t i0[kUpdateUnroll];
     bool full[kUpdateUnroll];
@@ -369,7 +537,7 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
 }
 
 template <typename GT>
-__global__ void __launch_bounds__(kUpdateThreads)
+__global__ void __launch_bounds__(kUpdateThreads, kUpdateMinBlocks)
     adamw_update_kernel(const GT* __restrict__ g, uint64_t n, uint64_t elem_base,
                         float* __restrict__ master, float* __restrict__ mom,
                         float* __restrict__ var, uint16_t* __restrict__ w16,
@@ -446,7 +614,9 @@ cudaError_t launch_norm_partials(int dtype, const void* grads, uint64_t n, uint6
                                  DeviceStepState* st, const FinalizeParams& fp, int grid,
                                  cudaStream_t stream) {
   if (n_chunks == 0) return cudaErrorInvalidValue;
-  const unsigned blocks = static_cast<unsigned>(grid < int(n_chunks) ? grid : int(n_chunks));
+  // One block per chunk: the block scheduler balances the ragged last wave.
+  (void)grid;
+  const unsigned blocks = n_chunks;
   if (dtype == 0)
     norm_partials_kernel<float><<<blocks, kTreeThreads, 0, stream>>>(
         static_cast<const float*>(grads), n, chunk_begin, n_chunks, scaler, partials, st, fp);
@@ -472,6 +642,31 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
     adamw_update_kernel<uint16_t><<<blocks, kUpdateThreads, 0, stream>>>(
         static_cast<const uint16_t*>(grads), n, elem_base, master, moment, variance, w16,
         offsets, decay, tile_first_tensor, p, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero1_reduce(int dtype, const void* recv, uint32_t ranks, uint64_t stride,
+                                uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
+                                const FinalizeParams& fp, float* gsum, double* send,
+                                DeviceStepState* st, int grid, cudaStream_t stream) {
+  if (n_chunks == 0) return cudaErrorInvalidValue;
+  const unsigned blocks = static_cast<unsigned>(grid < int(n_chunks) ? grid : int(n_chunks));
+  if (dtype == 0)
+    zero1_reduce_kernel<float><<<blocks, kTreeThreads, 0, stream>>>(
+        static_cast<const float*>(recv), ranks, stride, n_valid, n_chunks, scaler, fp, gsum, send,
+        st);
+  else
+    zero1_reduce_kernel<uint16_t><<<blocks, kTreeThreads, 0, stream>>>(
+        static_cast<const uint16_t*>(recv), ranks, stride, n_valid, n_chunks, scaler, fp, gsum,
+        send, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero1_finalize(const double* gathered, uint32_t ranks, uint32_t per_rank,
+                                  DeviceScaler* scaler, DeviceStepState* st,
+                                  const FinalizeParams& fp, cudaStream_t stream) {
+  zero1_finalize_kernel<<<1, kTreeThreads, 0, stream>>>(gathered, ranks, per_rank, scaler, st,
+                                                        fp);
   return cudaGetLastError();
 }
 

@@ -22,10 +22,26 @@ constexpr uint32_t kTreeThreads = 256;
 constexpr uint32_t kVec = 8;
 constexpr uint32_t kChunkIters = kChunkElems / (kTreeThreads * kVec);  // 32
 
-// Update kernel tiling: one 256-thread block step covers kTileElems elements.
+// Update kernel tiling: one 256-thread block step covers kTileElems elements
+// (kUpdateUnroll 8-element vectors per thread).  The build may override the
+// unroll, the minimum resident blocks per SM (register cap) and how many of
+// its own tiles ahead a block bulk-prefetches into L2.
+#ifndef SLM_UPDATE_UNROLL
+#define SLM_UPDATE_UNROLL 2
+#endif
+#ifndef SLM_UPDATE_MIN_BLOCKS
+#define SLM_UPDATE_MIN_BLOCKS 1
+#endif
+#ifndef SLM_UPDATE_PREFETCH
+#define SLM_UPDATE_PREFETCH 0
+#endif
 constexpr uint32_t kUpdateThreads = 256;
-constexpr uint32_t kUpdateUnroll = 2;
-constexpr uint32_t kTileElems = kUpdateThreads * kVec * kUpdateUnroll;  // 4096
+constexpr uint32_t kUpdateUnroll = SLM_UPDATE_UNROLL;
+constexpr uint32_t kUpdateMinBlocks = SLM_UPDATE_MIN_BLOCKS;
+constexpr uint32_t kUpdatePrefetch = SLM_UPDATE_PREFETCH;
+constexpr uint32_t kTileElems = kUpdateThreads * kVec * kUpdateUnroll;
+// Norm pass: vector loads issued together before their squares are added.
+constexpr uint32_t kNormBatch = 8;
 
 struct DeviceScaler {
   float scale;
@@ -90,6 +106,16 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 const uint64_t* offsets, const uint8_t* decay,
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
                                 DeviceStepState* st, int grid, cudaStream_t stream);
+// ZeRO-1: rank-ordered sum of the received gradient slices + unscale + chunk
+// partials (send[n_chunks] receives the non-finite flag), then the finalize of
+// the all-gathered partials.
+cudaError_t launch_zero1_reduce(int dtype, const void* recv, uint32_t ranks, uint64_t stride,
+                                uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
+                                const FinalizeParams& fp, float* gsum, double* send,
+                                DeviceStepState* st, int grid, cudaStream_t stream);
+cudaError_t launch_zero1_finalize(const double* gathered, uint32_t ranks, uint32_t per_rank,
+                                  DeviceScaler* scaler, DeviceStepState* st,
+                                  const FinalizeParams& fp, cudaStream_t stream);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

@@ -127,6 +127,10 @@ SIGNATURES = [
     ("slm_opt_norm_pass", _I, [_P, _P, _I, _I, ctypes.POINTER(StepConfig), _P]),
     ("slm_opt_update_pass", _I, [_P, ctypes.POINTER(StepConfig), _P]),
     ("slm_opt_apply_update", _I, [_P, _P, _U64, _F, _U64, _U64, ctypes.c_char_p]),
+    ("slm_zero1_unique_id", _I, [_P]),
+    ("slm_opt_create_zero1", _I, [ctypes.POINTER(TensorSpec), _U32, _I, _I, _I, _P, _U32,
+                                  ctypes.POINTER(_P)]),
+    ("slm_opt_shard_range", _I, [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
     ("slm_opt_set_loss_scale", _I, [_P, _F, _U32]),
     ("slm_opt_get_loss_scale", _I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_U32)]),
     ("slm_canonical_learning_rate", _I, [_U64, ctypes.POINTER(_F)]),

@@ -27,8 +27,8 @@ INCLUDE = REPO_ROOT / "include"
 LIB_NAME = "libslmopt.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["kernels.cu", "api.cu", "sha256.cpp"]
-HEADERS = ["slmopt_internal.h", "sha256.h"]
+SOURCES = ["kernels.cu", "api.cu", "zero1.cu", "sha256.cpp"]
+HEADERS = ["slmopt_internal.h", "handle.h", "sha256.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -52,6 +52,20 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found: the CUDA toolkit is required to build libslmopt.so")
 
 
+def nccl_paths() -> tuple[Path, Path]:
+    """(include dir, lib dir) of the NCCL that torch ships (the one a torch
+    process has loaded), else the system NCCL."""
+    try:
+        import nvidia.nccl  # namespace package from the nvidia-nccl wheel
+
+        root = Path(list(nvidia.nccl.__path__)[0])
+        if (root / "include" / "nccl.h").exists() and (root / "lib" / "libnccl.so.2").exists():
+            return root / "include", root / "lib"
+    except Exception:
+        pass
+    return Path("/usr/include"), Path("/usr/lib/x86_64-linux-gnu")
+
+
 def _inputs() -> list[Path]:
     return [CSRC / s for s in SOURCES] + [CSRC / h for h in HEADERS] + [INCLUDE / "slmopt.h"]
 
@@ -68,13 +82,15 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     if not force and not is_stale():
         return LIB_PATH
     out_tmp = LIB_PATH.with_suffix(".so.tmp")
+    nccl_inc, nccl_lib = nccl_paths()
     cmd = (
         [nvcc_path()]
         + ARCH_FLAGS
         + NVCC_FLAGS
         + (extra_flags or [])
-        + ["-I", str(INCLUDE), "-o", str(out_tmp)]
+        + ["-I", str(INCLUDE), "-I", str(nccl_inc), "-o", str(out_tmp)]
         + [str(CSRC / s) for s in SOURCES]
+        + ["-L", str(nccl_lib), "-l:libnccl.so.2", "-Xlinker", f"-rpath={nccl_lib}"]
     )
     if verbose:
         print(" ".join(cmd), file=sys.stderr)

@@ -1,0 +1,205 @@
+"""ZeRO-1 data-parallel optimizer step: partition math, the per-rank handle,
+and the multi-GPU benchmark driver.
+
+The reference runs one device per process and has no collective
+(src/train/cuda_backend.rs:56-73); this path is new.  Every rank holds the
+master/m/v of one chunk-aligned shard of the flat PARAM-001 buffer plus the
+full bf16 weights; one step exchanges gradient slices, sums them in rank order,
+agrees on one norm, updates its shard and all-gathers the bf16 weights (the
+collectives run inside libslmopt.so over NCCL).  The result is bit-identical to
+a single replica's step on the rank-ordered f32 sum of all ranks' gradients.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import statistics
+from dataclasses import dataclass
+
+from . import _lib
+from .layout import TensorTable
+from .optimizer import B200Adamw
+
+CHUNK = 65536
+
+
+@dataclass(frozen=True)
+class Partition:
+    """Chunk-aligned shards of a P-element flat buffer over `world` ranks."""
+
+    P: int
+    world: int
+    chunks: int
+    chunks_per_rank: int
+
+    @property
+    def stride(self) -> int:
+        """Padded elements per rank (a whole number of chunks)."""
+        return self.chunks_per_rank * CHUNK
+
+    def shard(self, rank: int) -> tuple[int, int]:
+        """(begin, length) of rank's elements; length may be 0 for tiny P."""
+        begin = rank * self.stride
+        return begin, max(0, min(self.stride, self.P - begin))
+
+    def padded_chunks(self) -> int:
+        return self.chunks_per_rank * self.world
+
+
+def partition(P: int, world: int) -> Partition:
+    if P <= 0 or world <= 0:
+        raise ValueError("P and world must be positive")
+    chunks = (P + CHUNK - 1) // CHUNK
+    return Partition(P, world, chunks, (chunks + world - 1) // world)
+
+
+def unique_id() -> bytes:
+    """A fresh NCCL unique id for rank 0 to broadcast."""
+    buf = (ctypes.c_uint8 * 128)()
+    _lib.check(_lib.load().slm_zero1_unique_id(buf))
+    return bytes(buf)
+
+
+class Zero1Adamw(B200Adamw):
+    """One rank's ZeRO-1 optimizer handle (collective calls: construction,
+    step, init_master, read_state, state_sha256 -- every rank in the same order)."""
+
+    def __init__(self, table: TensorTable, rank: int, world: int, uid: bytes, device: int = 0,
+                 timeout_ms: int = 0):
+        self.lib = _lib.load()
+        self.table = table
+        self.device = device
+        self.rank = rank
+        self.world = world
+        specs = (_lib.TensorSpec * len(table))()
+        self._names = [n.encode() for n in table.names]
+        for i, (name, n, dec) in enumerate(zip(self._names, table.elements, table.decay)):
+            specs[i].name = name
+            specs[i].elements = n
+            specs[i].weight_decay = 1 if dec else 0
+        if len(uid) != 128:
+            raise ValueError("the NCCL unique id is 128 bytes")
+        idbuf = (ctypes.c_uint8 * 128)(*uid)
+        h = ctypes.c_void_p()
+        _lib.check(self.lib.slm_opt_create_zero1(specs, len(table), device, rank, world, idbuf,
+                                                 timeout_ms, ctypes.byref(h)))
+        self._h = h
+        self.P = int(self.lib.slm_opt_parameter_count(h))
+
+    def shard_range(self) -> tuple[int, int]:
+        b, n = ctypes.c_uint64(), ctypes.c_uint64()
+        self._check(self.lib.slm_opt_shard_range(self._h, ctypes.byref(b), ctypes.byref(n)))
+        return int(b.value), int(n.value)
+
+
+# ---- multi-GPU benchmark (bench.py --gpus N under torchrun) ----------------------------
+def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> None:
+    """ZeRO-1 step on N GPUs: every rank holds its own seeded bf16 gradient
+    (seed = rank) x 65,536; value = P / (max over ranks of the step time)."""
+    import json
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from . import synth
+    from .layout import GqaDimensions
+    from .optimizer import StepOptions
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if world < 2:
+        raise SystemExit("the ZeRO-1 bench needs torchrun with WORLD_SIZE >= 2")
+    torch.cuda.set_device(local)
+    # Host-side plumbing only (barriers, the id broadcast, the max over ranks);
+    # the step's collectives run on libslmopt's own NCCL communicator.
+    dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    P = table.parameter_count
+    ids = [unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    opt = Zero1Adamw(table, rank, world, ids[0], device=local, timeout_ms=120000)
+    state = synth.optimizer_state(P, 0)
+    opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
+                   validate=False)
+    opt.validate()
+    opt.set_loss_scale(65536.0)
+    grads = synth.grads_bf16(P, seed=rank)
+    dev = torch.from_numpy(grads).cuda()
+    opts = StepOptions(learning_rate=3e-4, one_based_update=10,
+                       loss_scale_mode=_lib.SCALE_DYNAMIC)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        opt.step(dev, opts, stream=stream, wait=False)
+    first = opt.read_result()
+    if first.status != 0 or first.skipped:
+        raise RuntimeError(f"warm-up step failed on rank {rank}: {first.as_dict()}")
+    K = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        smi_id = f"GPU-{torch.cuda.get_device_properties(local).uuid}".replace("GPU-GPU-", "GPU-")
+    except Exception:
+        smi_id = str(local)
+    clocks = clock_sampler(smi_id) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start.record(stream)
+    for _ in range(K):
+        opt.step(dev, opts, stream=stream, wait=False)
+    end.record(stream)
+    res = opt.read_result()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms_local = start.elapsed_time(end) / K
+    t = torch.tensor([ms_local], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if res.status != 0 or res.skipped:
+        raise RuntimeError(f"timed step failed on rank {rank}: {res.as_dict()}")
+
+    # End to end: the gradient from pinned host memory each step, result read back.
+    host = torch.from_numpy(grads).pin_memory()
+    E = max(3, args.e2e_steps)
+    opt.step(host, opts, stream=stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(E):
+        opt.step(host, opts, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / E], dtype=torch.float64)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    opt.close()
+    dist.barrier()
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        part = partition(P, world)
+        nvlink_bytes = 2 * 2 * part.stride * (world - 1)  # grads in + weights in, per rank
+        line = {
+            "metric": metric, "value": P / (ms * 1e-3), "unit": unit, "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded numpy Philox normals; rank r uses seed r)",
+            "config": workload_config(args, world, P, len(table)),
+            "roofline": {"bound": "nvlink", "achieved": nvlink_bytes / (ms * 1e-3) / 1e9,
+                         "peak": 770.0, "unit": "GB/s",
+                         "frac": nvlink_bytes / (ms * 1e-3) / 1e9 / 770.0, "traffic": None,
+                         "peak_source": "measured peer copy per direction (pool figure)",
+                         "nvlink_bytes_per_rank": nvlink_bytes,
+                         "hbm_peak_gbs": peak, "hbm_peak_source": peak_kind},
+            "e2e": {"value": P / (e2e_ms * 1e-3), "unit": unit,
+                    "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 64,
+                    "ms_per_step": e2e_ms},
+            "gpu_launches": 3 * K,
+            "clocks": clk,
+            "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale},
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()

@@ -1,0 +1,145 @@
+"""ZeRO-1 over NCCL on real GPUs: one child process per GPU, each driving its
+rank through the C ABI; the gathered state must equal the oracle's single
+replica step on the rank-ordered f32 sum of all ranks' bf16 gradients, bit for
+bit, and an injected inf on one rank must make every rank skip.  Needs >= 2
+visible GPUs (skipped otherwise)."""
+from __future__ import annotations
+
+import hashlib
+import multiprocessing as mp
+import os
+import socket
+import time
+import traceback
+
+import numpy as np
+import pytest
+
+import slm_oracle as oracle
+from slmopt import GqaDimensions, TensorTable, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:
+        return 0
+
+
+def _digest(state: dict) -> dict:
+    return {k: hashlib.sha256(state[k].tobytes()).hexdigest() for k in state}
+
+
+def _rank_main(rank, world, port, table_name, out_q):
+    try:
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from slmopt import StepOptions, _lib
+        from slmopt.zero1 import Zero1Adamw, unique_id
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=120))
+        table = _table(table_name)
+        P = table.parameter_count
+        ids = [unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        opt = Zero1Adamw(table, rank, world, ids[0], device=rank, timeout_ms=120000)
+        st = synth.optimizer_state(P, 0)
+        opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+        opt.set_loss_scale(65536.0)
+        grads = synth.grads_bf16(P, seed=rank)
+        opts = StepOptions(learning_rate=3e-4, one_based_update=10,
+                           loss_scale_mode=_lib.SCALE_DYNAMIC)
+        r1 = opt.step(torch.from_numpy(grads).cuda(), opts)
+        state1 = opt.read_state()  # collective gather
+        sha1 = opt.state_sha256()  # collective
+        bad = grads.copy()
+        if rank == world - 1:
+            synth.inject_nonfinite(bad, 5, table.offsets)
+        r2 = opt.step(torch.from_numpy(bad).cuda(), StepOptions(
+            learning_rate=3e-4, one_based_update=11, loss_scale_mode=_lib.SCALE_DYNAMIC))
+        state2 = opt.read_state()
+        scale = opt.loss_scale()
+        opt.close()
+        out_q.put((rank, {"r1": r1.as_dict(), "r2": r2.as_dict(), "d1": _digest(state1),
+                          "d2": _digest(state2), "sha1": sha1, "scale": scale,
+                          "bf16": hashlib.sha256(state1["bf16"].tobytes()).hexdigest()}))
+        dist.destroy_process_group()
+    except Exception:
+        out_q.put((rank, {"error": traceback.format_exc()}))
+
+
+def _table(name: str) -> TensorTable:
+    if name == "smoke":
+        return TensorTable.from_dimensions(GqaDimensions.smoke())
+    if name == "135m":
+        return TensorTable.from_dimensions(GqaDimensions.canonical())
+    return TensorTable.from_sizes([65536 * 5 + 17, 768, 4096 + 3], [True, False, True])
+
+
+def _run(world: int, table_name: str, timeout: float = 600):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, table_name, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    deadline = time.time() + timeout
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, payload = q.get(timeout=2.0)
+            res[r] = payload
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+@pytest.mark.parametrize("table_name", ["ragged", "smoke", "135m"])
+def test_zero1_equals_single_replica(table_name):
+    n = _gpus()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(n, 8) if table_name != "ragged" else 2
+    res = _run(world, table_name)
+    assert len(res) == world, res
+    for r, p in res.items():
+        assert "error" not in p, p["error"]
+    table = _table(table_name)
+    P = table.parameter_count
+    grads = [synth.grads_bf16(P, seed=r) for r in range(world)]
+    gsum = oracle.rank_sum_bf16(grads, threads=8)
+    state = synth.optimizer_state(P, 0)
+    scaler = oracle.Scaler(65536.0, 0)
+    ref = oracle.step(oracle.make_config(lr=3e-4, t=10, dynamic=True), gsum, table.offsets,
+                      table.decay, state, scaler, threads=8)
+    want = _digest(state)
+    want_sha = oracle.state_sha256(table.names, table.offsets, table.decay, state)[1]
+    for r, p in res.items():
+        assert p["r1"]["status"] == 0 and p["r1"]["skipped"] == 0
+        assert p["r1"]["sum_squares"] == ref.sum_squares
+        assert np.float32(p["r1"]["clip_scale"]) == np.float32(ref.clip_scale)
+        assert p["d1"] == want, f"rank {r} state differs from the single replica"
+        assert p["sha1"] == want_sha
+        # the injected inf on the last rank makes every rank skip
+        assert p["r2"]["skipped"] == 1 and p["r2"]["nonfinite"] == 1
+        assert p["r2"]["next_loss_scale"] == 32768.0 and p["scale"][0] == 32768.0
+        assert p["d2"] == p["d1"]

@@ -234,6 +234,30 @@ int slm_opt_create_zero1(const slm_tensor_spec* table, uint32_t n_tensors, int d
 /* This rank's element range [begin, begin + len) of the flat buffer. */
 int slm_opt_shard_range(const slm_opt_handle* h, uint64_t* begin, uint64_t* len);
 
+/* ---- gradient norm without allocation -----------------------------------------
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc
+ * where they need the norm (another allocator owns the HBM budget, a latency-
+ * critical loop must not take cudaMalloc's device-wide synchronisation, or all
+ * memory is reserved up front): the fixed-tree f64 norm, clip scale and
+ * non-finite flag of `n` gradients of `dtype` on the current device, divided by
+ * `loss_scale` -- the same values an optimizer handle's norm pass computes.
+ * Its scratch is a fixed file-scope device array (about 33 KB on every GPU that
+ * loads the library, held until exit), so nothing is allocated; n above
+ * SLM_NOALLOC_MAX_ELEMENTS is rejected with SLM_ERR_SIZE_LIMIT.  The result is
+ * written to the caller's device memory `out_device`, stream-ordered on
+ * `stream`.  The first call on a device looks up the array's device address,
+ * so make that first call before any stream capture.  All calls on a device
+ * share the array: calls whose work overlaps on the GPU race. */
+#define SLM_NOALLOC_MAX_ELEMENTS 268435456ull /* 2^28 elements = 4,096 chunks */
+typedef struct slm_norm_result {
+    double sum_squares;  /* fixed-tree f64 sum of (g / loss_scale)^2 */
+    double grad_norm;    /* sqrt(sum_squares) */
+    float clip_scale;    /* min(max_grad_norm / sqrtf((float)sum), 1); 1 when the sum is 0 */
+    uint32_t nonfinite;  /* 1 when a gradient or the f32 sum is inf/nan (clip_scale is then 0) */
+} slm_norm_result;
+int slm_grad_norm_noalloc(const void* grads, int dtype, uint64_t n, float loss_scale,
+                          float max_grad_norm, slm_norm_result* out_device, void* stream);
+
 /* ---- loss scaler ------------------------------------------------------------- */
 int slm_opt_set_loss_scale(slm_opt_handle* h, float scale, uint32_t good_steps);
 int slm_opt_get_loss_scale(slm_opt_handle* h, float* scale, uint32_t* good_steps);

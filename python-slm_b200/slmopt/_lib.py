@@ -99,6 +99,19 @@ class StepResult(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class NormResult(ctypes.Structure):
+    """slm_norm_result (written to device memory by slm_grad_norm_noalloc)."""
+
+    _fields_ = [
+        ("sum_squares", ctypes.c_double),
+        ("grad_norm", ctypes.c_double),
+        ("clip_scale", ctypes.c_float),
+        ("nonfinite", ctypes.c_uint32),
+    ]
+
+
+NOALLOC_MAX_ELEMENTS = 268435456
+
 _P = ctypes.c_void_p
 _U64 = ctypes.c_uint64
 _U32 = ctypes.c_uint32
@@ -131,6 +144,7 @@ SIGNATURES = [
     ("slm_opt_create_zero1", _I, [ctypes.POINTER(TensorSpec), _U32, _I, _I, _I, _P, _U32,
                                   ctypes.POINTER(_P)]),
     ("slm_opt_shard_range", _I, [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
+    ("slm_grad_norm_noalloc", _I, [_P, _I, _U64, _F, _F, _P, _P]),
     ("slm_opt_set_loss_scale", _I, [_P, _F, _U32]),
     ("slm_opt_get_loss_scale", _I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_U32)]),
     ("slm_canonical_learning_rate", _I, [_U64, ctypes.POINTER(_F)]),

@@ -44,10 +44,10 @@ FALLBACK_HBM_GBS = 6650.0
 # read g (2 or 4) + master/m/v (12), write master/m/v (12) + bf16 (2).
 UPDATE_BYTES = {"mixed": 28, "fp32": 30}
 STEP_BYTES = {"mixed": 30, "fp32": 34}  # + the norm pass's read of g
-# dram__bytes_read.sum + dram__bytes_write.sum of one update-kernel launch from
-# the ncu capture summarised under profiles/ (scaled to the full 135M launch);
-# None until a capture exists for the current kernel.
-UPDATE_TRAFFIC_BYTES = {"mixed": None, "fp32": None}
+# dram__bytes_read.sum + dram__bytes_write.sum of one update-kernel launch,
+# from one ncu capture of a 33,554,432-parameter prefix scaled by parameter
+# count to the full launch; None where no capture exists.
+UPDATE_TRAFFIC_BYTES = {"mixed": 3.555e9, "fp32": None}
 
 
 def parse_args():
@@ -334,7 +334,7 @@ def run_single(args) -> None:
     traffic = UPDATE_TRAFFIC_BYTES[args.workload]
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "kernel": "adamw_update_kernel", "peak_source": peak_kind,
+                "kernel": "adamw_update_bulk_kernel", "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": UPDATE_BYTES[args.workload] * P,
                 "kernel_ms": upd_ms, "norm_pass_ms": norm_ms,
                 "step_gbs": STEP_BYTES[args.workload] * P / (ms * 1e-3) / 1e9}
@@ -356,7 +356,7 @@ def run_single(args) -> None:
     e2e_ms = e0.elapsed_time(e1) / E
     wall_ms = (time.perf_counter() - t0) * 1e3 / E
     e2e = {"value": P / (e2e_ms * 1e-3), "unit": UNIT,
-           "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 64,
+           "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 80,
            "ms_per_step": e2e_ms, "wall_ms_per_step": wall_ms}
 
     line = {

@@ -234,6 +234,24 @@ int slm_opt_create_zero1(const slm_tensor_spec* table, uint32_t n_tensors, int d
 /* This rank's element range [begin, begin + len) of the flat buffer. */
 int slm_opt_shard_range(const slm_opt_handle* h, uint64_t* begin, uint64_t* len);
 
+/* How a ZeRO-1 step moves data between ranks.  SLM_ZERO1_PEER (the default
+ * when every rank could map every other rank's buffers with CUDA IPC at
+ * creation): the reduce kernel reads the other ranks' gradient slices over
+ * NVLink directly from their registered gradient buffers, the update kernel
+ * stores its bf16 results straight into every rank's weights, and ranks meet
+ * at bounded device-side flag barriers.  SLM_ZERO1_NCCL: NCCL send/recv and
+ * all-gathers with a staging buffer.  Both give bit-identical results. */
+typedef enum slm_zero1_exchange { SLM_ZERO1_NCCL = 0, SLM_ZERO1_PEER = 1 } slm_zero1_exchange;
+/* Collective: every rank must select the same exchange before its next step.
+ * SLM_ZERO1_PEER fails with SLM_ERR_INVALID_ARGUMENT if it was not set up. */
+int slm_opt_zero1_set_exchange(slm_opt_handle* h, int exchange);
+int slm_opt_zero1_exchange(const slm_opt_handle* h);
+/* The rank's registered gradient buffer (bytes = 4P; holds P bf16 or P f32
+ * gradients).  A step given this pointer reads it in place (the other ranks
+ * read their slices of it); any other gradient pointer is first copied into
+ * it.  Do not overwrite it while a step that reads it is in flight. */
+int slm_opt_gradient_buffer(slm_opt_handle* h, void** out_device_ptr, uint64_t* bytes);
+
 /* ---- gradient norm without allocation -----------------------------------------
  * No counterpart in the reference.  For callers that cannot call cudaMalloc
  * where they need the norm (another allocator owns the HBM budget, a latency-

@@ -100,6 +100,9 @@ void fill_result(const DeviceStepState& s, slm_step_result* out) {
   out->status = s.status != 0 ? s.status
                               : (s.result_nonfinite ? SLM_ERR_MODEL_OPTIMIZER_RESULT_NONFINITE
                                                     : SLM_OK);
+  // A bounded in-kernel wait gave up: a peer never arrived (2) or a copy
+  // pipeline stalled (1).
+  if (s.kernel_error) out->status = (s.kernel_error & 2u) ? SLM_ERR_TIMEOUT : SLM_ERR_INTERNAL;
 }
 
 int read_state(slm_opt_handle* h, cudaStream_t s, DeviceStepState* out) {
@@ -268,6 +271,7 @@ int enqueue_update(slm_opt_handle* h, const void* dev_grads, int dtype,
 
 int finish_result(slm_opt_handle* h, const DeviceStepState& ds, slm_step_result* out) {
   fill_result(ds, out);
+  if (ds.kernel_error) h->broken = true;  // the ranks may be out of step: re-create the handle
   if (out->status != SLM_OK)
     return h->err(out->status, std::string("optimizer step failed: ") +
                                    slm_status_code_string(out->status));

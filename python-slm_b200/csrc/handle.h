@@ -96,6 +96,14 @@ struct slm_opt_handle {
   double* d_gathered = nullptr;    // world * (chunks_per_rank + 1)
   uint32_t timeout_ms = 0;
   bool broken = false;             // a collective timed out and the comm was aborted
+  // Peer-memory exchange (default when every rank could map every other
+  // rank's buffers with CUDA IPC; otherwise the NCCL exchange above).
+  int exchange = 0;                // SLM_ZERO1_NCCL or SLM_ZERO1_PEER
+  void* d_gradbuf = nullptr;       // registered gradient buffer, P * 4 bytes, exported
+  uint32_t* d_flags = nullptr;     // kFlagSlots * kMaxRanks arrival epochs, exported
+  slmopt::PeerTable peers{};       // every rank's buffers as mapped here (own included)
+  void* opened[slmopt::kMaxRanks][4] = {};  // IPC mappings to close on destroy
+  uint32_t epoch = 0;              // step counter shared (implicitly) by all ranks
 
   bool sharded() const { return world > 1; }
 
@@ -126,5 +134,6 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
 int zero1_wait(slm_opt_handle* h, cudaStream_t s);
 int zero1_gather(slm_opt_handle* h, const void* shard_src, size_t elem_bytes, void* dst_full,
                  cudaStream_t s);
+int setup_peer_exchange(slm_opt_handle* h, cudaStream_t s);
 void zero1_release(slm_opt_handle* h);
 }  // namespace slmopt

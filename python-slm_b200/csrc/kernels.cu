@@ -126,40 +126,65 @@ __device__ __forceinline__ double block_fold(double v, double* warp_sums) {
   return r;
 }
 
-__device__ __forceinline__ void load_full8(const float* __restrict__ g, float (&x)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(g));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(g + 4));
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-}
+// Raw 8-element vectors, kept packed while a batch of loads is in flight.
+template <typename GT>
+struct RawVec;
+template <>
+struct RawVec<uint16_t> {
+  uint4 r;
+  __device__ __forceinline__ void load(const uint16_t* p) {
+    r = __ldg(reinterpret_cast<const uint4*>(p));
+  }
+  __device__ __forceinline__ void unpack(float (&x)[8]) const { unpack_bf16x8(r, x); }
+};
+template <>
+struct RawVec<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  }
+  __device__ __forceinline__ void unpack(float (&x)[8]) const {
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+};
 
-__device__ __forceinline__ void load_full8(const uint16_t* __restrict__ g, float (&x)[8]) {
-  unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(g)), x);
+// Adds the exact f64 squares of 8 unscaled values to acc, in order.  d*d is
+// exact in f64 (24-bit significands), so each FMA rounds once, exactly like
+// acc + d*d.  (Widening f32 -> f64 with integer bit placement instead of the
+// hardware conversion was measured slower: it made the pass ALU-bound.)
+template <bool kMul>
+__device__ __forceinline__ double add_squares8(double acc, float (&x)[8], const ScaleInfo& sc) {
+#pragma unroll
+  for (uint32_t j = 0; j < kVec; ++j) {
+    const double d = static_cast<double>(unscale<kMul>(x[j], sc));
+    acc = __fma_rn(d, d, acc);
+  }
+  return acc;
 }
 
 template <typename GT, bool kMul>
 __device__ __forceinline__ double chunk_thread_sum(const GT* __restrict__ g, uint64_t base,
                                                    uint64_t n, const ScaleInfo& sc) {
+  // 128 bytes of gradient per thread in flight per batch.
+  constexpr uint32_t kBatch = sizeof(GT) == 2 ? kNormBatch : kNormBatch / 2;
   double acc = 0.0;
   if (base + kChunkElems <= n) {
-    // Whole chunk in range: kNormBatch unguarded loads go out together, then
+    // Whole chunk in range: kBatch unguarded loads go out together, then
     // their squares are added in the tree's element order.
     const GT* p = g + base + static_cast<uint64_t>(threadIdx.x) * kVec;
 #pragma unroll 1
-    for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kNormBatch) {
-      float x[kNormBatch][kVec];
+    for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kBatch) {
+      RawVec<GT> raw[kBatch];
 #pragma unroll
-      for (uint32_t b = 0; b < kNormBatch; ++b)
-        load_full8(p + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec), x[b]);
+      for (uint32_t b = 0; b < kBatch; ++b)
+        raw[b].load(p + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec));
 #pragma unroll
-      for (uint32_t b = 0; b < kNormBatch; ++b) {
-#pragma unroll
-        for (uint32_t j = 0; j < kVec; ++j) {
-          const double d = static_cast<double>(unscale<kMul>(x[b][j], sc));
-          // d*d is exact in f64 (24-bit significands), so the FMA rounds
-          // once, exactly like acc + d*d.
-          acc = __fma_rn(d, d, acc);
-        }
+      for (uint32_t b = 0; b < kBatch; ++b) {
+        float x[kVec];
+        raw[b].unpack(x);
+        acc = add_squares8<kMul>(acc, x, sc);
       }
     }
     return acc;
@@ -259,7 +284,7 @@ __device__ void finalize_block(const PartialsView& partials, uint32_t nonfinite,
 }
 
 template <typename GT>
-__global__ void __launch_bounds__(kTreeThreads)
+__global__ void __launch_bounds__(kTreeThreads, 3)
     norm_partials_kernel(const GT* __restrict__ g, uint64_t n, uint64_t chunk_begin,
                          uint32_t n_chunks, DeviceScaler* scaler, double* __restrict__ partials,
                          DeviceStepState* st, FinalizeParams fp) {
@@ -325,11 +350,7 @@ __device__ __forceinline__ double zero1_thread_sum(const GT* __restrict__ recv, 
     } else {
       for (uint32_t j = 0; j < kVec && e0 + j < n; ++j) gsum[e0 + j] = s[j];
     }
-#pragma unroll
-    for (uint32_t j = 0; j < kVec; ++j) {
-      const double d = static_cast<double>(unscale<kMul>(s[j], sc));
-      acc = __fma_rn(d, d, acc);
-    }
+    acc = add_squares8<kMul>(acc, s, sc);
   }
   return acc;
 }
@@ -452,7 +473,7 @@ __device__ __forceinline__ float decay_of(uint64_t e, uint32_t& k,
   return __ldg(decay + k) ? p.decay_weight : p.no_decay_weight;
 }
 
-template <typename GT, bool kMul>
+template <typename GT, bool kMul, bool kPeers>
 __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n,
                                             uint64_t elem_base, float* __restrict__ master,
                                             float* __restrict__ mom, float* __restrict__ var,
@@ -461,7 +482,7 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
                                             const uint8_t* __restrict__ decay,
                                             const uint32_t* __restrict__ tile_first,
                                             const AdamwParams& p, const ScaleInfo& sc,
-                                            float clip) {
+                                            float clip, const PeerStores& ps) {
   bool bad = false;
   const uint64_t n_tiles = (n + kTileElems - 1) / kTileElems;
   if constexpr (kUpdatePrefetch > 0) {
@@ -517,6 +538,11 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
         packed.z = bits[4] | (bits[5] << 16);
         packed.w = bits[6] | (bits[7] << 16);
         __stcs(reinterpret_cast<uint4*>(w16 + i0[u]), packed);
+        if constexpr (kPeers) {
+#pragma unroll
+          for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+            if (q < ps.count) __stcs(reinterpret_cast<uint4*>(ps.w16[q] + i0[u]), packed);
+        }
       } else if (i0[u] < n) {
         // Ragged tail: scalar accesses for the last < 8 elements.
         for (uint32_t j = 0; j < kVec && i0[u] + j < n; ++j) {
@@ -529,6 +555,11 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
           mom[i] = m;
           var[i] = v;
           w16[i] = bf16_rne_bits(t1);
+          if constexpr (kPeers) {
+#pragma unroll
+            for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+              if (q < ps.count) ps.w16[q][i] = bf16_rne_bits(t1);
+          }
         }
       }
     }
@@ -536,24 +567,273 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
   return bad;
 }
 
-template <typename GT>
+template <typename GT, bool kPeers>
 __global__ void __launch_bounds__(kUpdateThreads, kUpdateMinBlocks)
     adamw_update_kernel(const GT* __restrict__ g, uint64_t n, uint64_t elem_base,
                         float* __restrict__ master, float* __restrict__ mom,
                         float* __restrict__ var, uint16_t* __restrict__ w16,
                         const uint64_t* __restrict__ offsets, const uint8_t* __restrict__ decay,
                         const uint32_t* __restrict__ tile_first, AdamwParams p,
-                        DeviceStepState* st) {
+                        DeviceStepState* st, PeerStores ps) {
   // Written by the previous kernel on this stream; uniform for the grid.
-  if (st->skipped) return;
+  if (st->skipped || st->kernel_error) return;
   const ScaleInfo sc = decode_scale(st->loss_scale_used);
   const float clip = st->clip_apply;
   const bool bad =
-      sc.mul ? update_loop<GT, true>(g, n, elem_base, master, mom, var, w16, offsets, decay,
-                                     tile_first, p, sc, clip)
-             : update_loop<GT, false>(g, n, elem_base, master, mom, var, w16, offsets, decay,
-                                      tile_first, p, sc, clip);
+      sc.mul ? update_loop<GT, true, kPeers>(g, n, elem_base, master, mom, var, w16, offsets,
+                                             decay, tile_first, p, sc, clip, ps)
+             : update_loop<GT, false, kPeers>(g, n, elem_base, master, mom, var, w16, offsets,
+                                              decay, tile_first, p, sc, clip, ps);
   if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(&st->result_nonfinite, 1u);
+  if constexpr (kPeers) __threadfence_system();  // peer stores visible before the closing barrier
+}
+
+// ---- bulk-copy pipelined update (SLM_UPDATE_BULK=1) ---------------------------
+// Register pressure caps the plain kernel at two resident blocks per SM, so
+// only ~2 tiles of loads per SM are in flight.  Here a producer warp moves each
+// 2,048-element tile of g / master / m / v from HBM into one of kBulkStages
+// shared-memory stages with cp.async.bulk (completion counted in bytes on an
+// mbarrier), and 8 consumer warps compute from shared memory and stream the
+// results straight to global memory; in-flight bytes no longer cost registers.
+// Consumer thread t owns elements [4t, 4t+4) and [1024+4t, 1024+4t+4) of a
+// tile, so its shared-memory reads and its global stores are conflict-free and
+// coalesced.  Every wait is bounded (a few seconds of %globaltimer); on expiry
+// the kernel records kernel_error and leaves instead of hanging.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity; false after ~4 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u && global_ns() - t0 > 4000000000ull) return false;
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <typename GT>
+struct BulkStage {
+  static constexpr uint32_t kG = kBulkTile * sizeof(GT);
+  static constexpr uint32_t kF = kBulkTile * 4;
+  static constexpr uint32_t kBytes = kG + 3 * kF;
+};
+
+template <typename GT>
+constexpr size_t bulk_smem_bytes() {
+  return size_t(kBulkStages) * BulkStage<GT>::kBytes + 2 * kBulkStages * sizeof(uint64_t);
+}
+
+__device__ __forceinline__ void lds4(const float* p, float (&x)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+}
+
+__device__ __forceinline__ void lds_grad4(const float* p, float (&x)[4]) { lds4(p, x); }
+__device__ __forceinline__ void lds_grad4(const uint16_t* p, float (&x)[4]) {
+  const uint2 r = *reinterpret_cast<const uint2*>(p);
+  x[0] = __uint_as_float(r.x << 16);
+  x[1] = __uint_as_float(r.x & 0xffff0000u);
+  x[2] = __uint_as_float(r.y << 16);
+  x[3] = __uint_as_float(r.y & 0xffff0000u);
+}
+
+// AdamW on 4 consecutive local elements starting at i (global elem_base + i)
+// whose g / master / m / v are already in registers; streams the results out.
+template <bool kMul, bool kPeers>
+__device__ __forceinline__ void update4(uint64_t i, uint64_t elem_base, float (&gx)[4],
+                                        float (&th)[4], float (&mm)[4], float (&vv)[4],
+                                        float* __restrict__ master, float* __restrict__ mom,
+                                        float* __restrict__ var, uint16_t* __restrict__ w16,
+                                        const uint64_t* __restrict__ offsets,
+                                        const uint8_t* __restrict__ decay, uint32_t k,
+                                        const AdamwParams& p, const ScaleInfo& sc, float clip,
+                                        const PeerStores& ps, bool& bad) {
+  const uint64_t e0 = elem_base + i;
+  const float wd0 = decay_of(e0, k, offsets, decay, p);
+  const bool uniform = e0 + 4 <= __ldg(offsets + k + 1);
+  uint32_t bits[4];
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const float wd = uniform ? wd0 : decay_of(e0 + j, k, offsets, decay, p);
+    const float gv = __fmul_rn(unscale<kMul>(gx[j], sc), clip);
+    th[j] = adamw_elem(th[j], gv, mm[j], vv[j], wd, p, bad);
+    bits[j] = bf16_rne_bits(th[j]);
+  }
+  __stcs(reinterpret_cast<float4*>(master + i), make_float4(th[0], th[1], th[2], th[3]));
+  __stcs(reinterpret_cast<float4*>(mom + i), make_float4(mm[0], mm[1], mm[2], mm[3]));
+  __stcs(reinterpret_cast<float4*>(var + i), make_float4(vv[0], vv[1], vv[2], vv[3]));
+  const uint2 packed = make_uint2(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16));
+  __stcs(reinterpret_cast<uint2*>(w16 + i), packed);
+  if constexpr (kPeers) {
+#pragma unroll
+    for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+      if (q < ps.count) __stcs(reinterpret_cast<uint2*>(ps.w16[q] + i), packed);
+  }
+}
+
+template <typename GT, bool kMul, bool kPeers>
+__device__ __forceinline__ bool bulk_consume(uint8_t* smem, uint64_t* full_bar,
+                                             uint64_t* empty_bar, uint64_t n_full,
+                                             uint64_t elem_base, float* __restrict__ master,
+                                             float* __restrict__ mom, float* __restrict__ var,
+                                             uint16_t* __restrict__ w16,
+                                             const uint64_t* __restrict__ offsets,
+                                             const uint8_t* __restrict__ decay,
+                                             const uint32_t* __restrict__ tile_first,
+                                             const AdamwParams& p, const ScaleInfo& sc,
+                                             float clip, const PeerStores& ps, bool& bad) {
+  using Stage = BulkStage<GT>;
+  const uint32_t t = threadIdx.x;
+  uint32_t i = 0;
+  for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
+    const uint32_t s = i % kBulkStages;
+    if (!mbar_wait(&full_bar[s], (i / kBulkStages) & 1u)) return false;
+    const uint8_t* base = smem + size_t(s) * Stage::kBytes;
+    const GT* sg = reinterpret_cast<const GT*>(base);
+    const float* sm = reinterpret_cast<const float*>(base + Stage::kG);
+    const float* s1 = sm + kBulkTile;
+    const float* s2 = s1 + kBulkTile;
+    const uint64_t tile0 = tile * kBulkTile;
+    const uint32_t k = __ldg(tile_first + tile0 / kTileElems);
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+      const uint32_t o = h * (kBulkTile / 2) + 4 * t;
+      float gx[4], th[4], mm[4], vv[4];
+      lds_grad4(sg + o, gx);
+      lds4(sm + o, th);
+      lds4(s1 + o, mm);
+      lds4(s2 + o, vv);
+      update4<kMul, kPeers>(tile0 + o, elem_base, gx, th, mm, vv, master, mom, var, w16, offsets, decay,
+                    k, p, sc, clip, ps, bad);
+    }
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(&empty_bar[s]);
+  }
+  return true;
+}
+
+template <typename GT, bool kPeers>
+__global__ void __launch_bounds__(kBulkThreads)
+    adamw_update_bulk_kernel(const GT* __restrict__ g, uint64_t n, uint64_t elem_base,
+                             float* __restrict__ master, float* __restrict__ mom,
+                             float* __restrict__ var, uint16_t* __restrict__ w16,
+                             const uint64_t* __restrict__ offsets,
+                             const uint8_t* __restrict__ decay,
+                             const uint32_t* __restrict__ tile_first, AdamwParams p,
+                             DeviceStepState* st, PeerStores ps) {
+  using Stage = BulkStage<GT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  if (st->skipped || st->kernel_error) return;  // uniform for the grid
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(kBulkStages) * Stage::kBytes);
+  uint64_t* empty_bar = full_bar + kBulkStages;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kBulkStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kBulkConsumers / 32);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const ScaleInfo sc = decode_scale(st->loss_scale_used);
+  const float clip = st->clip_apply;
+  const uint64_t n_full = n / kBulkTile;
+  bool ok = true;
+  bool bad = false;
+  if (threadIdx.x >= kBulkConsumers) {
+    // Producer warp: lane 0 keeps kBulkStages tiles in flight.
+    if (threadIdx.x == kBulkConsumers) {
+      uint32_t i = 0;
+      for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
+        const uint32_t s = i % kBulkStages;
+        if (i >= kBulkStages && !mbar_wait(&empty_bar[s], ((i / kBulkStages) - 1u) & 1u)) {
+          ok = false;
+          break;
+        }
+        uint8_t* base = smem + size_t(s) * Stage::kBytes;
+        const uint64_t e0 = tile * kBulkTile;
+        mbar_arrive_expect_tx(&full_bar[s], Stage::kBytes);
+        bulk_load(base, g + e0, Stage::kG, &full_bar[s]);
+        bulk_load(base + Stage::kG, master + e0, Stage::kF, &full_bar[s]);
+        bulk_load(base + Stage::kG + Stage::kF, mom + e0, Stage::kF, &full_bar[s]);
+        bulk_load(base + Stage::kG + 2 * Stage::kF, var + e0, Stage::kF, &full_bar[s]);
+      }
+    }
+  } else {
+    ok = sc.mul ? bulk_consume<GT, true, kPeers>(smem, full_bar, empty_bar, n_full, elem_base, master,
+                                         mom, var, w16, offsets, decay, tile_first, p, sc, clip,
+                                         ps, bad)
+                : bulk_consume<GT, false, kPeers>(smem, full_bar, empty_bar, n_full, elem_base, master,
+                                          mom, var, w16, offsets, decay, tile_first, p, sc, clip,
+                                          ps, bad);
+    // Ragged tail after the last whole tile: element by element, block 0.
+    if (blockIdx.x == 0) {
+      for (uint64_t i = n_full * kBulkTile + threadIdx.x; i < n; i += kBulkConsumers) {
+        uint32_t k = __ldg(tile_first + i / kTileElems);
+        const float wd = decay_of(elem_base + i, k, offsets, decay, p);
+        const float gv = __fmul_rn(
+            sc.mul ? unscale<true>(ld_grad1(g, i), sc) : unscale<false>(ld_grad1(g, i), sc),
+            clip);
+        float m = mom[i], v = var[i];
+        const float t1 = adamw_elem(master[i], gv, m, v, wd, p, bad);
+        master[i] = t1;
+        mom[i] = m;
+        var[i] = v;
+        w16[i] = bf16_rne_bits(t1);
+        if constexpr (kPeers) {
+#pragma unroll
+          for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+            if (q < ps.count) ps.w16[q][i] = bf16_rne_bits(t1);
+        }
+      }
+    }
+  }
+  if (!ok) atomicOr(&st->kernel_error, 1u);
+  if (bad) atomicOr(&st->result_nonfinite, 1u);
+  if constexpr (kPeers) __threadfence_system();  // peer stores visible before the closing barrier
 }
 
 // ---- state initialisation / validation ----------------------------------------
@@ -579,6 +859,164 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
   if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(bad_flag, 1u);
 }
 
+// ---- ZeRO-1 over peer memory ------------------------------------------------------
+// Flag barrier between the ranks of one node: lane q announces this rank's
+// arrival (the step's epoch) in rank q's flag array, then waits until rank q
+// has announced itself here.  Epochs only grow, so flags are never reset; the
+// wait is bounded and records kernel_error instead of hanging.
+__global__ void peer_barrier_kernel(PeerTable pt, int rank, int world, uint32_t slot,
+                                    uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns) {
+  const int q = threadIdx.x;
+  __threadfence_system();
+  if (q < world)
+    *reinterpret_cast<volatile uint32_t*>(pt.flags[q] + slot * kMaxRanks + rank) = epoch;
+  if (q < world) {
+    const volatile uint32_t* mine = pt.flags[rank] + slot * kMaxRanks + q;
+    const uint64_t t0 = global_ns();
+    while (static_cast<int32_t>(*mine - epoch) < 0) {
+      if (global_ns() - t0 > timeout_ns) {
+        atomicOr(&st->kernel_error, 2u);
+        break;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+// The gradient slices of this rank's shard are read straight from every
+// rank's gradient buffer over NVLink (own slice locally), summed in rank order
+// 0..N-1, unscaled and reduced to chunk partials exactly like a single
+// replica.  The last block pushes this rank's partials and non-finite flag
+// into every rank's gathered area and raises their partials flag.
+template <typename GT, bool kMul>
+__device__ __forceinline__ double p2p_thread_sum(const PeerTable& pt, int world,
+                                                 uint64_t shard_begin, uint64_t base,
+                                                 uint64_t n, float* __restrict__ gsum,
+                                                 const ScaleInfo& sc) {
+  double acc = 0.0;
+  for (uint32_t k = 0; k < kChunkIters; ++k) {
+    const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
+                        static_cast<uint64_t>(threadIdx.x) * kVec;
+    if (e0 >= n) break;
+    float s[kVec];
+    if (e0 + kVec <= n) {
+      // Every rank's 16/32 bytes go out before any is added (packed meanwhile).
+      RawVec<GT> raw[kMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q)
+        if (q < world) raw[q].load(static_cast<const GT*>(pt.grads[q]) + shard_begin + e0);
+      raw[0].unpack(s);
+#pragma unroll
+      for (int q = 1; q < kMaxRanks; ++q)
+        if (q < world) {
+          float x[kVec];
+          raw[q].unpack(x);
+#pragma unroll
+          for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
+        }
+    } else {
+      load_grad8(static_cast<const GT*>(pt.grads[0]) + shard_begin, e0, n, s);
+      for (int q = 1; q < world; ++q) {
+        float x[kVec];
+        load_grad8(static_cast<const GT*>(pt.grads[q]) + shard_begin, e0, n, x);
+#pragma unroll
+        for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
+      }
+    }
+    if (e0 + kVec <= n) {
+      __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
+      __stcg(reinterpret_cast<float4*>(gsum + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
+    } else {
+      for (uint32_t j = 0; j < kVec && e0 + j < n; ++j) gsum[e0 + j] = s[j];
+    }
+    acc = add_squares8<kMul>(acc, s, sc);
+  }
+  return acc;
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kTreeThreads)
+    zero1_p2p_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
+                            uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
+                            FinalizeParams fp, float* __restrict__ gsum,
+                            double* __restrict__ send, uint32_t epoch, DeviceStepState* st) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  __shared__ uint32_t s_last;
+  if (st->kernel_error) return;  // a barrier of this step already gave up
+  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
+  bool bad = false;
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
+    const double acc =
+        sc.mul ? p2p_thread_sum<GT, true>(pt, world, shard_begin, base, n_valid, gsum, sc)
+               : p2p_thread_sum<GT, false>(pt, world, shard_begin, base, n_valid, gsum, sc);
+    bad |= !isfinite(acc);
+    const double total = block_fold(acc, warp_sums);
+    if (threadIdx.x == 0) send[c] = total;
+  }
+  const int any_bad = __syncthreads_or(bad ? 1 : 0);
+  if (threadIdx.x == 0) {
+    if (any_bad) atomicOr(&st->nonfinite_accum, 1u);
+    __threadfence();
+    s_last = (atomicAdd(&st->blocks_done, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (s_last == 0u) return;
+  __threadfence();
+  const double flag = st->nonfinite_accum != 0u ? 1.0 : 0.0;
+  const uint64_t slot = static_cast<uint64_t>(rank) * (n_chunks + 1);
+  for (int q = 0; q < world; ++q) {
+    double* dst = pt.gathered[q] + slot;
+    for (uint32_t c = threadIdx.x; c < n_chunks; c += kTreeThreads) dst[c] = __ldcg(send + c);
+    if (threadIdx.x == 0) dst[n_chunks] = flag;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < static_cast<unsigned>(world))
+    *reinterpret_cast<volatile uint32_t*>(pt.flags[threadIdx.x] + kSlotPartials * kMaxRanks +
+                                          rank) = epoch;
+  if (threadIdx.x == 0) {
+    st->nonfinite_accum = 0u;
+    st->blocks_done = 0u;
+  }
+  __threadfence_system();
+}
+
+// Waits (bounded) until every rank delivered its partials, then reduces them
+// in global chunk order -- the same norm / clip / skip bits on every rank.
+__global__ void __launch_bounds__(kTreeThreads)
+    zero1_p2p_finalize_kernel(PeerTable pt, int rank, int world, uint32_t per_rank,
+                              uint32_t epoch, DeviceScaler* scaler, DeviceStepState* st,
+                              FinalizeParams fp, uint64_t timeout_ns) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  __shared__ uint32_t s_ok;
+  if (threadIdx.x == 0) s_ok = st->kernel_error == 0u ? 1u : 0u;
+  __syncthreads();
+  if (s_ok && threadIdx.x < static_cast<unsigned>(world)) {
+    const volatile uint32_t* f = pt.flags[rank] + kSlotPartials * kMaxRanks + threadIdx.x;
+    const uint64_t t0 = global_ns();
+    while (static_cast<int32_t>(*f - epoch) < 0) {
+      if (global_ns() - t0 > timeout_ns) {
+        atomicOr(&st->kernel_error, 2u);
+        s_ok = 0u;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  __threadfence_system();
+  const double* gathered = pt.gathered[rank];
+  uint32_t nonfinite = 0u;
+  if (threadIdx.x == 0)
+    for (int q = 0; q < world; ++q)
+      nonfinite |= __ldcg(gathered + static_cast<uint64_t>(q) * (per_rank + 1) + per_rank) != 0.0
+                       ? 1u
+                       : 0u;
+  finalize_block(PartialsView{gathered, per_rank, per_rank + 1}, nonfinite, st, scaler, fp,
+                 warp_sums);
+}
+
 int sm_count(int device) {
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
@@ -598,14 +1036,54 @@ int norm_partials_grid(int device) {
   return sm_count(device) * per_sm;
 }
 
-int adamw_update_grid(int device, int dtype) {
+namespace {
+template <typename GT, bool kPeers>
+void allow_bulk_smem() {
+  cudaFuncSetAttribute(adamw_update_bulk_kernel<GT, kPeers>,
+                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(bulk_smem_bytes<GT>()));
+}
+
+template <typename GT>
+int update_blocks_per_sm() {
   int per_sm = 0;
-  cudaError_t e =
-      dtype == 0 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                       &per_sm, adamw_update_kernel<float>, kUpdateThreads, 0)
-                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                       &per_sm, adamw_update_kernel<uint16_t>, kUpdateThreads, 0);
-  if (e != cudaSuccess || per_sm <= 0) per_sm = 2;
+  cudaError_t e;
+  if constexpr (kUpdateBulk) {
+    allow_bulk_smem<GT, false>();
+    allow_bulk_smem<GT, true>();
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, adamw_update_bulk_kernel<GT, false>, kBulkThreads, bulk_smem_bytes<GT>());
+  } else {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_update_kernel<GT, false>,
+                                                      kUpdateThreads, 0);
+  }
+  return (e != cudaSuccess || per_sm <= 0) ? (kUpdateBulk ? 1 : 2) : per_sm;
+}
+
+template <typename GT, bool kPeers>
+void launch_update_typed(const void* grads, uint64_t n, uint64_t elem_base, float* master,
+                         float* moment, float* variance, uint16_t* w16, const uint64_t* offsets,
+                         const uint8_t* decay, const uint32_t* tile_first, const AdamwParams& p,
+                         DeviceStepState* st, int grid, cudaStream_t stream,
+                         const PeerStores& ps) {
+  const GT* g = static_cast<const GT*>(grads);
+  if constexpr (kUpdateBulk) {
+    const uint64_t tiles = n / kBulkTile;
+    const unsigned blocks =
+        static_cast<unsigned>(tiles == 0 ? 1 : (uint64_t(grid) < tiles ? uint64_t(grid) : tiles));
+    adamw_update_bulk_kernel<GT, kPeers><<<blocks, kBulkThreads, bulk_smem_bytes<GT>(), stream>>>(
+        g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st, ps);
+  } else {
+    const uint64_t tiles = (n + kTileElems - 1) / kTileElems;
+    const unsigned blocks =
+        static_cast<unsigned>(uint64_t(grid) < tiles ? uint64_t(grid) : tiles);
+    adamw_update_kernel<GT, kPeers><<<blocks, kUpdateThreads, 0, stream>>>(
+        g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st, ps);
+  }
+}
+}  // namespace
+
+int adamw_update_grid(int device, int dtype) {
+  const int per_sm = dtype == 0 ? update_blocks_per_sm<float>() : update_blocks_per_sm<uint16_t>();
   return sm_count(device) * per_sm;
 }
 
@@ -630,18 +1108,28 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 float* master, float* moment, float* variance, uint16_t* w16,
                                 const uint64_t* offsets, const uint8_t* decay,
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
-                                DeviceStepState* st, int grid, cudaStream_t stream) {
-  const uint64_t tiles = (n + kTileElems - 1) / kTileElems;
-  if (tiles == 0) return cudaSuccess;
-  const unsigned blocks = static_cast<unsigned>(uint64_t(grid) < tiles ? uint64_t(grid) : tiles);
-  if (dtype == 0)
-    adamw_update_kernel<float><<<blocks, kUpdateThreads, 0, stream>>>(
-        static_cast<const float*>(grads), n, elem_base, master, moment, variance, w16, offsets,
-        decay, tile_first_tensor, p, st);
-  else
-    adamw_update_kernel<uint16_t><<<blocks, kUpdateThreads, 0, stream>>>(
-        static_cast<const uint16_t*>(grads), n, elem_base, master, moment, variance, w16,
-        offsets, decay, tile_first_tensor, p, st);
+                                DeviceStepState* st, int grid, cudaStream_t stream,
+                                const PeerStores* peers) {
+  if (n == 0) return cudaSuccess;
+  const PeerStores ps = peers ? *peers : PeerStores{};
+  const bool with_peers = ps.count > 0;
+  if (dtype == 0) {
+    if (with_peers)
+      launch_update_typed<float, true>(grads, n, elem_base, master, moment, variance, w16, offsets,
+                                       decay, tile_first_tensor, p, st, grid, stream, ps);
+    else
+      launch_update_typed<float, false>(grads, n, elem_base, master, moment, variance, w16,
+                                        offsets, decay, tile_first_tensor, p, st, grid, stream, ps);
+  } else {
+    if (with_peers)
+      launch_update_typed<uint16_t, true>(grads, n, elem_base, master, moment, variance, w16,
+                                          offsets, decay, tile_first_tensor, p, st, grid, stream,
+                                          ps);
+    else
+      launch_update_typed<uint16_t, false>(grads, n, elem_base, master, moment, variance, w16,
+                                           offsets, decay, tile_first_tensor, p, st, grid, stream,
+                                           ps);
+  }
   return cudaGetLastError();
 }
 
@@ -667,6 +1155,37 @@ cudaError_t launch_zero1_finalize(const double* gathered, uint32_t ranks, uint32
                                   const FinalizeParams& fp, cudaStream_t stream) {
   zero1_finalize_kernel<<<1, kTreeThreads, 0, stream>>>(gathered, ranks, per_rank, scaler, st,
                                                         fp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_peer_barrier(const PeerTable& pt, int rank, int world, uint32_t slot,
+                                uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns,
+                                cudaStream_t stream) {
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(pt, rank, world, slot, epoch, st, timeout_ns);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero1_p2p_reduce(int dtype, const PeerTable& pt, int rank, int world,
+                                    uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
+                                    const DeviceScaler* scaler, const FinalizeParams& fp,
+                                    float* gsum, double* send, uint32_t epoch,
+                                    DeviceStepState* st, cudaStream_t stream) {
+  if (n_chunks == 0) return cudaErrorInvalidValue;
+  if (dtype == 0)
+    zero1_p2p_reduce_kernel<float><<<n_chunks, kTreeThreads, 0, stream>>>(
+        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st);
+  else
+    zero1_p2p_reduce_kernel<uint16_t><<<n_chunks, kTreeThreads, 0, stream>>>(
+        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero1_p2p_finalize(const PeerTable& pt, int rank, int world,
+                                      uint32_t per_rank, uint32_t epoch, DeviceScaler* scaler,
+                                      DeviceStepState* st, const FinalizeParams& fp,
+                                      uint64_t timeout_ns, cudaStream_t stream) {
+  zero1_p2p_finalize_kernel<<<1, kTreeThreads, 0, stream>>>(pt, rank, world, per_rank, epoch,
+                                                            scaler, st, fp, timeout_ns);
   return cudaGetLastError();
 }
 

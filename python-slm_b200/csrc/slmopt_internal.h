@@ -40,6 +40,20 @@ constexpr uint32_t kUpdateUnroll = SLM_UPDATE_UNROLL;
 constexpr uint32_t kUpdateMinBlocks = SLM_UPDATE_MIN_BLOCKS;
 constexpr uint32_t kUpdatePrefetch = SLM_UPDATE_PREFETCH;
 constexpr uint32_t kTileElems = kUpdateThreads * kVec * kUpdateUnroll;
+// Bulk-copy update kernel (SLM_UPDATE_BULK=1): a producer warp streams
+// 2,048-element tiles of g / master / m / v into a ring of shared-memory stages
+// with cp.async.bulk; 8 consumer warps compute from shared memory.
+#ifndef SLM_UPDATE_BULK
+#define SLM_UPDATE_BULK 1
+#endif
+#ifndef SLM_BULK_STAGES
+#define SLM_BULK_STAGES 2
+#endif
+constexpr uint32_t kBulkTile = 2048;
+constexpr uint32_t kBulkConsumers = 256;
+constexpr uint32_t kBulkThreads = kBulkConsumers + 32;
+constexpr uint32_t kBulkStages = SLM_BULK_STAGES;
+constexpr bool kUpdateBulk = SLM_UPDATE_BULK != 0;
 // Norm pass: vector loads issued together before their squares are added.
 constexpr uint32_t kNormBatch = 8;
 
@@ -68,6 +82,31 @@ struct __align__(16) DeviceStepState {
   // its last block, so every launch starts from zero without a memset.
   uint32_t nonfinite_accum;
   uint32_t blocks_done;
+  // Set when a bounded in-kernel wait gave up (never expected; reported as an
+  // internal error instead of hanging the GPU).
+  uint32_t kernel_error;
+  uint32_t reserved[3];
+};
+
+// ZeRO-1 over peer memory: device addresses (mapped into this process with
+// CUDA IPC) of every rank's gradient buffer, gathered-partials area, flag
+// array and bf16 weights; index = rank, own buffers included.
+constexpr int kMaxRanks = 8;
+constexpr uint32_t kSlotGrads = 0;     // gradients of this step are written
+constexpr uint32_t kSlotPartials = 1;  // partials delivered; peers done reading my gradients
+constexpr uint32_t kSlotWeights = 2;   // bf16 weights delivered
+constexpr uint32_t kFlagSlots = 3;
+struct PeerTable {
+  const void* grads[kMaxRanks];
+  double* gathered[kMaxRanks];
+  uint32_t* flags[kMaxRanks];
+  uint16_t* w16[kMaxRanks];
+};
+// bf16 destinations an update kernel also writes (the peers' weight buffers at
+// this shard's offset); count 0 for a single replica.
+struct PeerStores {
+  uint16_t* w16[kMaxRanks];
+  uint32_t count;
 };
 
 struct FinalizeParams {
@@ -105,7 +144,21 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 float* master, float* moment, float* variance, uint16_t* w16,
                                 const uint64_t* offsets, const uint8_t* decay,
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
-                                DeviceStepState* st, int grid, cudaStream_t stream);
+                                DeviceStepState* st, int grid, cudaStream_t stream,
+                                const PeerStores* peers = nullptr);
+// ZeRO-1 over peer memory (see zero1.cu).
+cudaError_t launch_peer_barrier(const PeerTable& pt, int rank, int world, uint32_t slot,
+                                uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns,
+                                cudaStream_t stream);
+cudaError_t launch_zero1_p2p_reduce(int dtype, const PeerTable& pt, int rank, int world,
+                                    uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
+                                    const DeviceScaler* scaler, const FinalizeParams& fp,
+                                    float* gsum, double* send, uint32_t epoch,
+                                    DeviceStepState* st, cudaStream_t stream);
+cudaError_t launch_zero1_p2p_finalize(const PeerTable& pt, int rank, int world,
+                                      uint32_t per_rank, uint32_t epoch, DeviceScaler* scaler,
+                                      DeviceStepState* st, const FinalizeParams& fp,
+                                      uint64_t timeout_ns, cudaStream_t stream);
 // ZeRO-1: rank-ordered sum of the received gradient slices + unscale + chunk
 // partials (send[n_chunks] receives the non-finite flag), then the finalize of
 // the all-gathered partials.

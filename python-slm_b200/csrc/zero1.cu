@@ -30,6 +30,7 @@
 #include <chrono>
 #include <new>
 #include <thread>
+#include <vector>
 
 using namespace slmopt;
 
@@ -114,14 +115,24 @@ void zero1_release(slm_opt_handle* h) {
       ncclCommDestroy(comm_of(h));
     h->comm = nullptr;
   }
+  for (int q = 0; q < kMaxRanks; ++q)
+    for (int b = 0; b < 4; ++b)
+      if (h->opened[q][b]) {
+        cudaIpcCloseMemHandle(h->opened[q][b]);
+        h->opened[q][b] = nullptr;
+      }
   cudaFree(h->d_recv);
   cudaFree(h->d_gsum);
   cudaFree(h->d_send);
   cudaFree(h->d_gathered);
+  cudaFree(h->d_gradbuf);
+  cudaFree(h->d_flags);
   h->d_recv = nullptr;
   h->d_gsum = nullptr;
   h->d_send = nullptr;
   h->d_gathered = nullptr;
+  h->d_gradbuf = nullptr;
+  h->d_flags = nullptr;
 }
 
 int zero1_gather(slm_opt_handle* h, const void* shard_src, size_t elem_bytes, void* dst_full,
@@ -157,6 +168,142 @@ int zero1_gather(slm_opt_handle* h, const void* shard_src, size_t elem_bytes, vo
   return st;
 }
 
+// Collective set-up of the peer-memory exchange: every rank exports its
+// gradient buffer, gathered-partials area, flag array and bf16 weights with
+// CUDA IPC, the 4 x 64-byte handles are all-gathered over NCCL, and each rank
+// maps the others'.  The ranks then agree (NCCL min) whether all of them
+// succeeded; if any did not, all use the NCCL exchange.
+int setup_peer_exchange(slm_opt_handle* h, cudaStream_t s) {
+  const int N = h->world;
+  h->exchange = SLM_ZERO1_NCCL;
+  if (N > kMaxRanks) return SLM_OK;
+  int st;
+  if ((st = h->cuda(cudaMalloc(&h->d_gradbuf, h->P * 4), "cudaMalloc gradient buffer"))) return st;
+  if ((st = h->cuda(cudaMalloc(&h->d_flags, kFlagSlots * kMaxRanks * sizeof(uint32_t)),
+                    "cudaMalloc flags")))
+    return st;
+  if ((st = h->cuda(cudaMemset(h->d_flags, 0, kFlagSlots * kMaxRanks * sizeof(uint32_t)),
+                    "memset flags")))
+    return st;
+  void* mine[4] = {h->d_gradbuf, h->d_gathered, h->d_flags, h->w16};
+  std::vector<cudaIpcMemHandle_t> handles(size_t(N) * 4);
+  int ok = 1;
+  for (int b = 0; b < 4; ++b)
+    if (cudaIpcGetMemHandle(&handles[size_t(h->rank) * 4 + b], mine[b]) != cudaSuccess) ok = 0;
+  cudaGetLastError();  // a refused export only selects the NCCL exchange
+  uint8_t* d_handles = nullptr;
+  int32_t* d_ok = nullptr;
+  const size_t hbytes = handles.size() * sizeof(cudaIpcMemHandle_t);
+  if ((st = h->cuda(cudaMalloc(&d_handles, hbytes), "cudaMalloc handle buffer"))) return st;
+  if ((st = h->cuda(cudaMalloc(&d_ok, sizeof(int32_t)), "cudaMalloc agreement"))) {
+    cudaFree(d_handles);
+    return st;
+  }
+  const size_t each = 4 * sizeof(cudaIpcMemHandle_t);
+  st = h->cuda(cudaMemcpy(d_handles + size_t(h->rank) * each, &handles[size_t(h->rank) * 4], each,
+                          cudaMemcpyHostToDevice),
+               "stage handles");
+  if (!st)
+    st = settle(h, ncclAllGather(d_handles + size_t(h->rank) * each, d_handles, each, ncclUint8,
+                                 comm_of(h), s),
+                "handle all-gather");
+  if (!st) st = zero1_wait(h, s);
+  if (!st)
+    st = h->cuda(cudaMemcpy(handles.data(), d_handles, hbytes, cudaMemcpyDeviceToHost),
+                 "fetch handles");
+  if (!st && ok) {
+    for (int q = 0; q < N && ok; ++q) {
+      if (q == h->rank) continue;
+      for (int b = 0; b < 4 && ok; ++b) {
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, handles[size_t(q) * 4 + b],
+                                 cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+          cudaGetLastError();
+          ok = 0;
+        } else {
+          h->opened[q][b] = ptr;
+        }
+      }
+    }
+  }
+  if (!st) {
+    const int32_t v = ok;
+    st = h->cuda(cudaMemcpy(d_ok, &v, sizeof(v), cudaMemcpyHostToDevice), "stage agreement");
+  }
+  if (!st)
+    st = settle(h, ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, comm_of(h), s),
+                "agreement all-reduce");
+  if (!st) st = zero1_wait(h, s);
+  int32_t all_ok = 0;
+  if (!st) st = h->cuda(cudaMemcpy(&all_ok, d_ok, sizeof(all_ok), cudaMemcpyDeviceToHost), "agree");
+  cudaFree(d_handles);
+  cudaFree(d_ok);
+  if (st) return st;
+  if (all_ok) {
+    for (int q = 0; q < N; ++q) {
+      void* const* src = q == h->rank ? mine : h->opened[q];
+      h->peers.grads[q] = src[0];
+      h->peers.gathered[q] = static_cast<double*>(src[1]);
+      h->peers.flags[q] = static_cast<uint32_t*>(src[2]);
+      h->peers.w16[q] = static_cast<uint16_t*>(src[3]);
+    }
+    h->exchange = SLM_ZERO1_PEER;
+  } else {
+    for (int q = 0; q < kMaxRanks; ++q)
+      for (int b = 0; b < 4; ++b)
+        if (h->opened[q][b]) {
+          cudaIpcCloseMemHandle(h->opened[q][b]);
+          h->opened[q][b] = nullptr;
+        }
+  }
+  return SLM_OK;
+}
+
+namespace {
+
+uint64_t barrier_timeout_ns(const slm_opt_handle* h) {
+  const uint64_t ms = h->timeout_ms < 10000u ? h->timeout_ms : 10000u;
+  return ms * 1000000ull;
+}
+
+// One ZeRO-1 step over peer memory, all on stream s (see slm_opt_zero1_set_exchange).
+int peer_step(slm_opt_handle* h, const void* dev, int dtype, const slm_step_config* cfg,
+              cudaStream_t s) {
+  const uint32_t epoch = ++h->epoch;
+  const uint64_t tmo = barrier_timeout_ns(h);
+  const FinalizeParams fp = finalize_params(h, cfg);
+  int st;
+  (void)dev;
+  if ((st = h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotGrads, epoch,
+                                        h->d_state, tmo, s),
+                    "gradient barrier")))
+    return st;
+  if ((st = h->cuda(launch_zero1_p2p_reduce(dtype, h->peers, h->rank, h->world, h->shard_begin,
+                                            h->shard_len, h->chunks_per_rank, h->d_scaler, fp,
+                                            h->d_gsum, h->d_send, epoch, h->d_state, s),
+                    "peer reduce kernel")))
+    return st;
+  if ((st = h->cuda(launch_zero1_p2p_finalize(h->peers, h->rank, h->world, h->chunks_per_rank,
+                                              epoch, h->d_scaler, h->d_state, fp, tmo, s),
+                    "peer finalize kernel")))
+    return st;
+  PeerStores ps{};
+  for (int q = 0; q < h->world; ++q)
+    if (q != h->rank) ps.w16[ps.count++] = h->peers.w16[q] + h->shard_begin;
+  const AdamwParams p = adamw_params(cfg);
+  if ((st = h->cuda(launch_adamw_update(SLM_DTYPE_F32, h->d_gsum, h->shard_len, h->shard_begin,
+                                        h->master, h->m1, h->m2, h->w16 + h->shard_begin,
+                                        h->d_offsets, h->d_decay, h->d_tile_first, p, h->d_state,
+                                        h->grid_update[0], s, &ps),
+                    "update kernel")))
+    return st;
+  return h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotWeights, epoch,
+                                     h->d_state, tmo, s),
+                 "weights barrier");
+}
+
+}  // namespace
+
 int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                const slm_step_config* cfg, cudaStream_t s) {
   if (h->broken || !h->comm)
@@ -165,6 +312,21 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
   const uint64_t S = h->shard_stride;
   const int N = h->world;
   int st;
+  if (memory != SLM_MEMORY_HOST && memory != SLM_MEMORY_DEVICE)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown memory kind");
+  if (memory == SLM_MEMORY_DEVICE && reinterpret_cast<uintptr_t>(grads) % 16 != 0)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "device gradients must be 16-byte aligned");
+  if (h->exchange == SLM_ZERO1_PEER) {
+    // The other ranks read this rank's slices from its registered buffer.
+    if (grads != h->d_gradbuf) {
+      const cudaMemcpyKind kind =
+          memory == SLM_MEMORY_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+      if ((st = h->cuda(cudaMemcpyAsync(h->d_gradbuf, grads, h->P * esize, kind, s),
+                        "gradient to registered buffer")))
+        return st;
+    }
+    return peer_step(h, h->d_gradbuf, dtype, cfg, s);
+  }
   // Stage host gradients on the device first.
   const void* dev = grads;
   if (memory == SLM_MEMORY_HOST) {
@@ -181,10 +343,6 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                       "gradient upload")))
       return st;
     dev = h->d_staging;
-  } else if (memory != SLM_MEMORY_DEVICE) {
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown memory kind");
-  } else if (reinterpret_cast<uintptr_t>(grads) % 16 != 0) {
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "device gradients must be 16-byte aligned");
   }
   const size_t need = size_t(N) * S * esize;
   if (h->recv_bytes < need) {
@@ -312,12 +470,39 @@ int slm_opt_create_zero1(const slm_tensor_spec* table, uint32_t n_tensors, int d
   ncclComm_t comm = nullptr;
   const ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &config);
   h->comm = comm;
-  if ((st = settle(h, r, "ncclCommInitRankConfig"))) {
+  if ((st = settle(h, r, "ncclCommInitRankConfig")) || (st = setup_peer_exchange(h, nullptr))) {
     const std::string msg = h->last_error;
     slm_opt_destroy(h);
     return fail(st, msg);
   }
   *out = h;
+  return SLM_OK;
+}
+
+int slm_opt_zero1_set_exchange(slm_opt_handle* h, int exchange) {
+  if (!h) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL handle");
+  if (!h->sharded()) return h->err(SLM_ERR_INVALID_ARGUMENT, "not a ZeRO-1 handle");
+  if (exchange == SLM_ZERO1_NCCL) {
+    h->exchange = SLM_ZERO1_NCCL;
+    return SLM_OK;
+  }
+  if (exchange == SLM_ZERO1_PEER && h->peers.flags[h->rank] != nullptr) {
+    h->exchange = SLM_ZERO1_PEER;
+    return SLM_OK;
+  }
+  return h->err(SLM_ERR_INVALID_ARGUMENT, "the peer-memory exchange is not available");
+}
+
+int slm_opt_zero1_exchange(const slm_opt_handle* h) {
+  return h && h->sharded() ? h->exchange : -1;
+}
+
+int slm_opt_gradient_buffer(slm_opt_handle* h, void** out_device_ptr, uint64_t* bytes) {
+  if (!h || !out_device_ptr || !bytes) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (!h->d_gradbuf)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "this handle has no registered gradient buffer");
+  *out_device_ptr = h->d_gradbuf;
+  *bytes = h->P * 4;
   return SLM_OK;
 }
 

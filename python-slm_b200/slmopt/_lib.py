@@ -51,6 +51,8 @@ NONFINITE_SKIP = 0
 NONFINITE_ERROR = 1
 SCALE_STATIC = 0
 SCALE_DYNAMIC = 1
+ZERO1_NCCL = 0
+ZERO1_PEER = 1
 
 
 class TensorSpec(ctypes.Structure):
@@ -144,6 +146,9 @@ SIGNATURES = [
     ("slm_opt_create_zero1", _I, [ctypes.POINTER(TensorSpec), _U32, _I, _I, _I, _P, _U32,
                                   ctypes.POINTER(_P)]),
     ("slm_opt_shard_range", _I, [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
+    ("slm_opt_zero1_set_exchange", _I, [_P, _I]),
+    ("slm_opt_zero1_exchange", _I, [_P]),
+    ("slm_opt_gradient_buffer", _I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_U64)]),
     ("slm_grad_norm_noalloc", _I, [_P, _I, _U64, _F, _F, _P, _P]),
     ("slm_opt_set_loss_scale", _I, [_P, _F, _U32]),
     ("slm_opt_get_loss_scale", _I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_U32)]),

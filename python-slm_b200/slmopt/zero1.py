@@ -91,6 +91,32 @@ class Zero1Adamw(B200Adamw):
         self._check(self.lib.slm_opt_shard_range(self._h, ctypes.byref(b), ctypes.byref(n)))
         return int(b.value), int(n.value)
 
+    @property
+    def exchange(self) -> int:
+        """_lib.ZERO1_PEER (peer-memory kernels) or _lib.ZERO1_NCCL."""
+        return int(self.lib.slm_opt_zero1_exchange(self._h))
+
+    def set_exchange(self, exchange: int) -> None:
+        """Collective: every rank selects the same exchange before its next step."""
+        self._check(self.lib.slm_opt_zero1_set_exchange(self._h, exchange))
+
+    def gradient_buffer(self, dtype: str = "bf16"):
+        """The registered gradient buffer as a CUDA tensor of P elements (bf16
+        bits as int16, or float32); a step given it reads it in place."""
+        import torch
+
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_uint64()
+        self._check(self.lib.slm_opt_gradient_buffer(self._h, ctypes.byref(ptr),
+                                                     ctypes.byref(nbytes)))
+        typestr = "<i2" if dtype == "bf16" else "<f4"
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (self.P,), "typestr": typestr,
+                                        "data": (int(ptr.value), False), "version": 3}
+
+        t = torch.as_tensor(_View(), device=f"cuda:{self.device}")
+        return t.view(torch.bfloat16) if dtype == "bf16" else t
+
 
 # ---- multi-GPU benchmark (bench.py --gpus N under torchrun) ----------------------------
 def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> None:
@@ -126,7 +152,12 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     opt.validate()
     opt.set_loss_scale(65536.0)
     grads = synth.grads_bf16(P, seed=rank)
-    dev = torch.from_numpy(grads).cuda()
+    if opt.exchange == _lib.ZERO1_PEER:
+        # write this rank's gradient where the other ranks read it
+        dev = opt.gradient_buffer("bf16")
+        dev.view(torch.int16).copy_(torch.from_numpy(grads.view("int16")))
+    else:
+        dev = torch.from_numpy(grads).cuda()
     opts = StepOptions(learning_rate=3e-4, one_based_update=10,
                        loss_scale_mode=_lib.SCALE_DYNAMIC)
     stream = torch.cuda.current_stream()
@@ -176,6 +207,7 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     te = torch.tensor([e0.elapsed_time(e1) / E], dtype=torch.float64)
     dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
+    opt_exchange = opt.exchange
     opt.close()
     dist.barrier()
     if rank == 0:
@@ -195,9 +227,10 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
                          "nvlink_bytes_per_rank": nvlink_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": peak_kind},
             "e2e": {"value": P / (e2e_ms * 1e-3), "unit": unit,
-                    "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 64,
+                    "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 80,
                     "ms_per_step": e2e_ms},
-            "gpu_launches": 3 * K,
+            "gpu_launches": (5 if opt_exchange == _lib.ZERO1_PEER else 3) * K,
+            "exchange": "peer-memory" if opt_exchange == _lib.ZERO1_PEER else "nccl",
             "clocks": clk,
             "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale},
         }

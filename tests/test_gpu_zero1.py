@@ -1,8 +1,8 @@
-"""ZeRO-1 over NCCL on real GPUs: one child process per GPU, each driving its
-rank through the C ABI; the gathered state must equal the oracle's single
-replica step on the rank-ordered f32 sum of all ranks' bf16 gradients, bit for
-bit, and an injected inf on one rank must make every rank skip.  Needs >= 2
-visible GPUs (skipped otherwise)."""
+"""ZeRO-1 on real GPUs, with both exchanges (peer memory over NVLink, and NCCL):
+one child process per GPU, each driving its rank through the C ABI; the
+gathered state must equal the oracle's single replica step on the rank-ordered
+f32 sum of all ranks' bf16 gradients, bit for bit, and an injected inf on one
+rank must make every rank skip.  Needs >= 2 visible GPUs (skipped otherwise)."""
 from __future__ import annotations
 
 import hashlib
@@ -34,7 +34,7 @@ def _digest(state: dict) -> dict:
     return {k: hashlib.sha256(state[k].tobytes()).hexdigest() for k in state}
 
 
-def _rank_main(rank, world, port, table_name, out_q):
+def _rank_main(rank, world, port, table_name, exchange, out_q):
     try:
         from datetime import timedelta
 
@@ -54,6 +54,9 @@ def _rank_main(rank, world, port, table_name, out_q):
         ids = [unique_id() if rank == 0 else None]
         dist.broadcast_object_list(ids, src=0)
         opt = Zero1Adamw(table, rank, world, ids[0], device=rank, timeout_ms=120000)
+        if exchange == "nccl":
+            opt.set_exchange(_lib.ZERO1_NCCL)
+        got_exchange = opt.exchange
         st = synth.optimizer_state(P, 0)
         opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
         opt.set_loss_scale(65536.0)
@@ -66,12 +69,23 @@ def _rank_main(rank, world, port, table_name, out_q):
         bad = grads.copy()
         if rank == world - 1:
             synth.inject_nonfinite(bad, 5, table.offsets)
-        r2 = opt.step(torch.from_numpy(bad).cuda(), StepOptions(
+        if got_exchange == _lib.ZERO1_PEER:
+            # write straight into the registered buffer the other ranks read
+            gbuf = opt.gradient_buffer("bf16")
+            gbuf.view(torch.int16).copy_(torch.from_numpy(bad.view(np.int16)))
+        else:
+            gbuf = torch.from_numpy(bad).cuda()
+        r2 = opt.step(gbuf, StepOptions(
             learning_rate=3e-4, one_based_update=11, loss_scale_mode=_lib.SCALE_DYNAMIC))
         state2 = opt.read_state()
+        # the same gradients from host memory skip again (scale halves again)
+        r3 = opt.step(bad, StepOptions(
+            learning_rate=3e-4, one_based_update=12, loss_scale_mode=_lib.SCALE_DYNAMIC))
+        state3 = opt.read_state()
         scale = opt.loss_scale()
         opt.close()
-        out_q.put((rank, {"r1": r1.as_dict(), "r2": r2.as_dict(), "d1": _digest(state1),
+        out_q.put((rank, {"exchange": got_exchange, "r1": r1.as_dict(), "r2": r2.as_dict(),
+                          "r3": r3.as_dict(), "d3": _digest(state3), "d1": _digest(state1),
                           "d2": _digest(state2), "sha1": sha1, "scale": scale,
                           "bf16": hashlib.sha256(state1["bf16"].tobytes()).hexdigest()}))
         dist.destroy_process_group()
@@ -87,13 +101,13 @@ def _table(name: str) -> TensorTable:
     return TensorTable.from_sizes([65536 * 5 + 17, 768, 4096 + 3], [True, False, True])
 
 
-def _run(world: int, table_name: str, timeout: float = 600):
+def _run(world: int, table_name: str, exchange: str, timeout: float = 600):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, table_name, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, table_name, exchange, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -113,13 +127,14 @@ def _run(world: int, table_name: str, timeout: float = 600):
     return res
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("table_name", ["ragged", "smoke", "135m"])
-def test_zero1_equals_single_replica(table_name):
+def test_zero1_equals_single_replica(table_name, exchange):
     n = _gpus()
     if n < 2:
         pytest.skip("needs at least 2 GPUs")
     world = min(n, 8) if table_name != "ragged" else 2
-    res = _run(world, table_name)
+    res = _run(world, table_name, exchange)
     assert len(res) == world, res
     for r, p in res.items():
         assert "error" not in p, p["error"]
@@ -133,7 +148,10 @@ def test_zero1_equals_single_replica(table_name):
                       table.decay, state, scaler, threads=8)
     want = _digest(state)
     want_sha = oracle.state_sha256(table.names, table.offsets, table.decay, state)[1]
+    from slmopt import _lib
+
     for r, p in res.items():
+        assert p["exchange"] == (_lib.ZERO1_PEER if exchange == "peer" else _lib.ZERO1_NCCL)
         assert p["r1"]["status"] == 0 and p["r1"]["skipped"] == 0
         assert p["r1"]["sum_squares"] == ref.sum_squares
         assert np.float32(p["r1"]["clip_scale"]) == np.float32(ref.clip_scale)
@@ -141,5 +159,7 @@ def test_zero1_equals_single_replica(table_name):
         assert p["sha1"] == want_sha
         # the injected inf on the last rank makes every rank skip
         assert p["r2"]["skipped"] == 1 and p["r2"]["nonfinite"] == 1
-        assert p["r2"]["next_loss_scale"] == 32768.0 and p["scale"][0] == 32768.0
+        assert p["r2"]["next_loss_scale"] == 32768.0
         assert p["d2"] == p["d1"]
+        assert p["r3"]["skipped"] == 1 and p["r3"]["next_loss_scale"] == 16384.0
+        assert p["scale"][0] == 16384.0 and p["d3"] == p["d1"]

@@ -59,6 +59,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["mixed", "fp32"], default="mixed")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="ZeRO-1 data movement: peer-memory kernels (default) or NCCL")
     ap.add_argument("--params", type=int, default=0,
                     help="profiling only: run on the first N parameters (whole 65,536-element "
                          "chunks) of the 135M layout instead of all of it")

@@ -209,6 +209,25 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
                          float learning_rate, uint64_t one_based_update,
                          uint64_t valid_targets, char* out_sha256_hex65);
 
+/* ---- micro-batch accumulation ---------------------------------------------------
+ * The reference sums each micro-batch's fp32 gradient into a host accumulator
+ * (src/train/trainer.rs:856-877, `total += value`) and normalises by the
+ * update's target count (:884).  On the device: slm_grad_accumulate adds
+ * `micro` (n elements of dtype, device memory) into the f32 accumulator in the
+ * same per-element order (overwrite=1 starts an update: acc = micro).  The last
+ * micro-batch of an update can instead go through slm_opt_norm_pass_accumulate,
+ * which accumulates and runs the norm pass over the sums in one read (unscale
+ * by cfg's loss scale -- the target count for the reference's normalisation
+ * -- non-finite check, fixed-tree norm, clip / skip); follow it with
+ * slm_opt_update_pass(h, cfg, stream), which reads `acc` as f32 gradients.
+ * A non-finite sum is caught by the norm pass (the reference stops at the
+ * micro-batch that produced it; the outcome -- no update -- is the same). */
+int slm_grad_accumulate(float* acc_device, const void* micro_device, int dtype, uint64_t n,
+                        int overwrite, void* stream);
+int slm_opt_norm_pass_accumulate(slm_opt_handle* h, float* acc_device, const void* micro,
+                                 int dtype, int memory, int overwrite,
+                                 const slm_step_config* cfg, void* stream);
+
 /* ---- ZeRO-1 data parallel (no counterpart in the reference, which runs one
  * device per process, src/train/cuda_backend.rs:56-73) ---------------------------
  * One handle per rank and GPU.  The flat buffer is cut into 65,536-element

@@ -272,7 +272,10 @@ void slmo_sha256(const void* data, uint64_t n, uint8_t out[32]) {
  * non-negative sum).  One chunk partial is formed exactly like a 256-thread
  * CUDA block does it:
  *   lane t (0..255) owns, for k = 0..31, the 8 consecutive elements starting
- *   at k*2048 + t*8, and adds their exact f64 squares in that order;
+ *   at k*2048 + t*8; it squares them in f32, sums the 8 squares pairwise in
+ *   f32 as ((q0+q1)+(q2+q3))+((q4+q5)+(q6+q7)) and adds that sum, in k order,
+ *   to its f64 accumulator (all terms are >= 0: the partial's relative error
+ *   stays below ~2.4e-7);
  *   each warp of 32 lanes folds with offsets 16,8,4,2,1 (lane l += lane l+off);
  *   the 8 warp results fold with offsets 4,2,1.
  * The total over chunk partials uses the same shape: lane t adds partials
@@ -304,13 +307,17 @@ static double chunk_partial_f32(const float* g, uint64_t n, uint64_t chunk, uint
         for (uint32_t k = 0; k < SLMO_CHUNK_ELEMS / (SLMO_TREE_THREADS * SLMO_TREE_VEC); ++k) {
             uint64_t e0 = base + (uint64_t)k * SLMO_TREE_THREADS * SLMO_TREE_VEC +
                           (uint64_t)t * SLMO_TREE_VEC;
+            if (e0 >= n) break;
+            float q[SLMO_TREE_VEC];
             for (uint32_t j = 0; j < SLMO_TREE_VEC; ++j) {
                 uint64_t e = e0 + j;
-                if (e >= n) break;
-                float x = g[e];
+                float x = e < n ? g[e] : 0.0f;
                 if (!is_finite_f32(x)) bad = 1;
-                acc = acc + (double)x * (double)x;
+                q[j] = x * x;
             }
+            float p = ((q[0] + q[1]) + (q[2] + q[3])) + ((q[4] + q[5]) + (q[6] + q[7]));
+            if (!is_finite_f32(p)) bad = 1;
+            acc = acc + (double)p;
         }
         lane[t] = acc;
     }

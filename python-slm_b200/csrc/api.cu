@@ -557,6 +557,50 @@ int slm_opt_norm_pass(slm_opt_handle* h, const void* grads, int dtype, int memor
   return SLM_OK;
 }
 
+int slm_grad_accumulate(float* acc_device, const void* micro_device, int dtype, uint64_t n,
+                        int overwrite, void* stream) {
+  if (!acc_device || !micro_device) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  if (reinterpret_cast<uintptr_t>(acc_device) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(micro_device) % 16 != 0)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "accumulator and gradients must be 16-byte aligned");
+  const cudaError_t e = launch_accumulate(dtype, acc_device, micro_device, n, overwrite,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(SLM_ERR_CUDA, std::string("accumulate kernel: ") + cudaGetErrorString(e));
+  return SLM_OK;
+}
+
+int slm_opt_norm_pass_accumulate(slm_opt_handle* h, float* acc_device, const void* micro,
+                                 int dtype, int memory, int overwrite,
+                                 const slm_step_config* cfg, void* stream) {
+  if (!h || !acc_device || !micro) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  if (h->sharded())
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "a ZeRO-1 handle runs whole steps (slm_opt_step)");
+  if (reinterpret_cast<uintptr_t>(acc_device) % 16 != 0)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "the accumulator must be 16-byte aligned");
+  int st = check_config(h, cfg);
+  if (st) return st;
+  DeviceGuard guard(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const void* dev = nullptr;
+  h->pass_grads = nullptr;
+  if ((st = stage_grads(h, micro, dtype, memory, s, &dev))) return st;
+  const FinalizeParams fp = finalize_params(h, cfg);
+  if ((st = h->cuda(launch_accumulate_norm(dtype, acc_device, dev, h->P, overwrite, h->n_chunks,
+                                           h->d_scaler, h->d_partials, h->d_state, fp, s),
+                    "accumulate + norm kernel")))
+    return st;
+  h->pass_grads = acc_device;
+  h->pass_dtype = SLM_DTYPE_F32;
+  h->pending = true;
+  h->pending_stream = s;
+  return SLM_OK;
+}
+
 int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* stream) {
   if (!h) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL handle");
   if (!h->pass_grads)

@@ -101,6 +101,11 @@ __device__ __forceinline__ void load_grad8(const uint16_t* __restrict__ g, uint6
   }
 }
 
+__device__ __forceinline__ float ld_grad1(const float* __restrict__ g, uint64_t i) { return g[i]; }
+__device__ __forceinline__ float ld_grad1(const uint16_t* __restrict__ g, uint64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(g[i]) << 16);
+}
+
 // ---- the fixed f64 tree -----------------------------------------------------
 // Folds one double per thread of a 256-thread block; result valid in thread 0.
 __device__ __forceinline__ double block_fold(double v, double* warp_sums) {
@@ -150,18 +155,24 @@ struct RawVec<float> {
   }
 };
 
-// Adds the exact f64 squares of 8 unscaled values to acc, in order.  d*d is
-// exact in f64 (24-bit significands), so each FMA rounds once, exactly like
-// acc + d*d.  (Widening f32 -> f64 with integer bit placement instead of the
-// hardware conversion was measured slower: it made the pass ALU-bound.)
+// One 8-element vector's contribution to a tree lane: the values are
+// unscaled, squared in f32, the 8 squares added pairwise in f32
+// ((q0+q1)+(q2+q3))+((q4+q5)+(q6+q7)), and that sum added to the lane's f64
+// accumulator.  Every term is >= 0, so the relative error of the partial stays
+// below ~2.4e-7 (4 f32 roundings); one f32 -> f64 conversion per 8 elements
+// keeps the conversion pipe off the critical path.  A non-finite or
+// overflowing value makes the sum non-finite.
 template <bool kMul>
 __device__ __forceinline__ double add_squares8(double acc, float (&x)[8], const ScaleInfo& sc) {
+  float q[kVec];
 #pragma unroll
   for (uint32_t j = 0; j < kVec; ++j) {
-    const double d = static_cast<double>(unscale<kMul>(x[j], sc));
-    acc = __fma_rn(d, d, acc);
+    const float u = unscale<kMul>(x[j], sc);
+    q[j] = __fmul_rn(u, u);
   }
-  return acc;
+  const float p = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3])),
+                            __fadd_rn(__fadd_rn(q[4], q[5]), __fadd_rn(q[6], q[7])));
+  return __dadd_rn(acc, static_cast<double>(p));
 }
 
 template <typename GT, bool kMul>
@@ -194,12 +205,8 @@ __device__ __forceinline__ double chunk_thread_sum(const GT* __restrict__ g, uin
                         static_cast<uint64_t>(threadIdx.x) * kVec;
     if (e0 >= n) break;  // the rest adds +0.0
     float x[kVec];
-    load_grad8(g, e0, n, x);
-#pragma unroll
-    for (uint32_t j = 0; j < kVec; ++j) {
-      const double d = static_cast<double>(unscale<kMul>(x[j], sc));
-      acc = __fma_rn(d, d, acc);
-    }
+    load_grad8(g, e0, n, x);  // zeros past n square to +0.0
+    acc = add_squares8<kMul>(acc, x, sc);
   }
   return acc;
 }
@@ -296,12 +303,122 @@ __global__ void __launch_bounds__(kTreeThreads, 3)
     const uint64_t chunk = chunk_begin + c;
     const uint64_t base = chunk * kChunkElems;
     // Squares are >= 0, so the partial is finite exactly when every unscaled
-    // element is finite (f32^2 * 65,536 cannot overflow f64).
+    // element and its f32 square is finite.
     const double acc = sc.mul ? chunk_thread_sum<GT, true>(g, base, n, sc)
                               : chunk_thread_sum<GT, false>(g, base, n, sc);
     bad |= !isfinite(acc);
     const double total = block_fold(acc, warp_sums);
     if (threadIdx.x == 0) partials[chunk] = total;
+  }
+  const int any_bad = __syncthreads_or(bad ? 1 : 0);
+  if (threadIdx.x == 0) {
+    if (any_bad) atomicOr(&st->nonfinite_accum, 1u);
+    __threadfence();
+    s_last = (atomicAdd(&st->blocks_done, 1u) == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (s_last == 0u) return;
+  __threadfence();
+  const uint32_t nonfinite =
+      threadIdx.x == 0 ? (atomicExch(&st->nonfinite_accum, 0u) != 0u ? 1u : 0u) : 0u;
+  finalize_block(PartialsView{partials, fp.total_chunks, fp.total_chunks}, nonfinite, st, scaler,
+                 fp, warp_sums);
+}
+
+// ---- micro-batch accumulation ----------------------------------------------------
+// acc[i] = acc[i] + micro[i] in f32, one micro-batch after another -- the
+// reference's host loop `total += value` (src/train/trainer.rs:865-877) moved
+// onto the device.  `overwrite` starts a new update (acc = micro).
+__device__ __forceinline__ void ld8f_stream(const float* __restrict__ p, float (&x)[8]) {
+  const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldcs(reinterpret_cast<const float4*>(p + 4));
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+template <typename GT>
+__device__ __forceinline__ void accumulate8(float* __restrict__ acc, const GT* __restrict__ micro,
+                                            uint64_t e0, uint64_t n, bool overwrite,
+                                            float (&s)[8]) {
+  if (e0 + kVec <= n) {
+    float x[kVec];
+    load_grad8(micro, e0, n, x);
+    if (overwrite) {
+#pragma unroll
+      for (uint32_t j = 0; j < kVec; ++j) s[j] = x[j];
+    } else {
+      ld8f_stream(acc + e0, s);
+#pragma unroll
+      for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
+    }
+    __stcs(reinterpret_cast<float4*>(acc + e0), make_float4(s[0], s[1], s[2], s[3]));
+    __stcs(reinterpret_cast<float4*>(acc + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+      const uint64_t i = e0 + j;
+      if (i < n) {
+        const float x = ld_grad1(micro, i);
+        s[j] = overwrite ? x : __fadd_rn(acc[i], x);
+        acc[i] = s[j];
+      } else {
+        s[j] = 0.0f;  // adds +0.0 to the partial
+      }
+    }
+  }
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(256)
+    accumulate_kernel(float* __restrict__ acc, const GT* __restrict__ micro, uint64_t n,
+                      int overwrite) {
+  const uint64_t vecs = (n + kVec - 1) / kVec;
+  for (uint64_t v = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; v < vecs;
+       v += uint64_t(gridDim.x) * blockDim.x) {
+    float s[kVec];
+    accumulate8(acc, micro, v * kVec, n, overwrite != 0, s);
+  }
+}
+
+// The last micro-batch fused with the norm pass: each element is accumulated
+// by the thread that owns it in the fixed tree, which then adds the square of
+// the unscaled sum -- the same partials norm_partials_kernel<float> would form
+// from the finished accumulator, without reading it again.
+template <typename GT, bool kMul>
+__device__ __forceinline__ double accum_thread_sum(float* __restrict__ acc,
+                                                   const GT* __restrict__ micro, uint64_t base,
+                                                   uint64_t n, bool overwrite,
+                                                   const ScaleInfo& sc) {
+  double a = 0.0;
+#pragma unroll 2
+  for (uint32_t k = 0; k < kChunkIters; ++k) {
+    const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
+                        static_cast<uint64_t>(threadIdx.x) * kVec;
+    if (e0 >= n) break;
+    float s[kVec];
+    accumulate8(acc, micro, e0, n, overwrite, s);
+    a = add_squares8<kMul>(a, s, sc);
+  }
+  return a;
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(kTreeThreads)
+    accumulate_norm_kernel(float* __restrict__ acc, const GT* __restrict__ micro, uint64_t n,
+                           int overwrite, uint32_t n_chunks, DeviceScaler* scaler,
+                           double* __restrict__ partials, DeviceStepState* st,
+                           FinalizeParams fp) {
+  __shared__ double warp_sums[kTreeThreads / 32];
+  __shared__ uint32_t s_last;
+  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
+  bool bad = false;
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
+    const double a = sc.mul ? accum_thread_sum<GT, true>(acc, micro, base, n, overwrite, sc)
+                            : accum_thread_sum<GT, false>(acc, micro, base, n, overwrite, sc);
+    bad |= !isfinite(a);
+    const double total = block_fold(a, warp_sums);
+    if (threadIdx.x == 0) partials[c] = total;
   }
   const int any_bad = __syncthreads_or(bad ? 1 : 0);
   if (threadIdx.x == 0) {
@@ -440,10 +557,6 @@ __device__ __forceinline__ void ld_grad8_stream(const uint16_t* __restrict__ g, 
   unpack_bf16x8(__ldcs(reinterpret_cast<const uint4*>(g)), x);
 }
 
-__device__ __forceinline__ float ld_grad1(const float* __restrict__ g, uint64_t i) { return g[i]; }
-__device__ __forceinline__ float ld_grad1(const uint16_t* __restrict__ g, uint64_t i) {
-  return __uint_as_float(static_cast<uint32_t>(g[i]) << 16);
-}
 
 // Bulk prefetch of [p, p + bytes) into L2 (no registers, no shared memory):
 // keeps the next tile's bytes in flight while this tile computes.  p and bytes
@@ -1186,6 +1299,36 @@ cudaError_t launch_zero1_p2p_finalize(const PeerTable& pt, int rank, int world,
                                       uint64_t timeout_ns, cudaStream_t stream) {
   zero1_p2p_finalize_kernel<<<1, kTreeThreads, 0, stream>>>(pt, rank, world, per_rank, epoch,
                                                             scaler, st, fp, timeout_ns);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_accumulate(int dtype, float* acc, const void* micro, uint64_t n,
+                              int overwrite, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const uint64_t vecs = (n + kVec - 1) / kVec;
+  const uint64_t want = (vecs + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>(want < 148u * 16u ? want : 148u * 16u);
+  if (dtype == 0)
+    accumulate_kernel<float><<<blocks, 256, 0, stream>>>(acc, static_cast<const float*>(micro),
+                                                         n, overwrite);
+  else
+    accumulate_kernel<uint16_t><<<blocks, 256, 0, stream>>>(
+        acc, static_cast<const uint16_t*>(micro), n, overwrite);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_accumulate_norm(int dtype, float* acc, const void* micro, uint64_t n,
+                                   int overwrite, uint32_t n_chunks, DeviceScaler* scaler,
+                                   double* partials, DeviceStepState* st,
+                                   const FinalizeParams& fp, cudaStream_t stream) {
+  if (n_chunks == 0) return cudaErrorInvalidValue;
+  if (dtype == 0)
+    accumulate_norm_kernel<float><<<n_chunks, kTreeThreads, 0, stream>>>(
+        acc, static_cast<const float*>(micro), n, overwrite, n_chunks, scaler, partials, st, fp);
+  else
+    accumulate_norm_kernel<uint16_t><<<n_chunks, kTreeThreads, 0, stream>>>(
+        acc, static_cast<const uint16_t*>(micro), n, overwrite, n_chunks, scaler, partials, st,
+        fp);
   return cudaGetLastError();
 }
 

@@ -47,8 +47,11 @@ __device__ __forceinline__ float grad_at(const uint16_t* g, uint64_t i) {
 }
 
 // The same reduction shape as the optimizer's norm pass: lane t of a 256-thread
-// block adds the exact f64 squares of its 8-element vectors at k*2048 + t*8
-// (k = 0..31), warps fold with offsets 16..1, the 8 warp sums with 4,2,1.
+// block takes its 8-element vectors at k*2048 + t*8 (k = 0..31); each vector's
+// unscaled values are squared in f32 and summed pairwise in f32
+// ((q0+q1)+(q2+q3))+((q4+q5)+(q6+q7)) (elements past n count as +0.0), and
+// that sum is added to the lane's f64 accumulator; warps fold with offsets
+// 16..1, the 8 warp sums with 4,2,1.
 __device__ __forceinline__ double fold256(double v, double* warp_sums) {
   for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(kFull, v, off));
   if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = v;
@@ -79,11 +82,15 @@ __global__ void __launch_bounds__(kTreeThreads)
     double acc = 0.0;
     for (uint32_t k = 0; k < kChunkIters; ++k) {
       const uint64_t e0 = base + uint64_t(k) * (kTreeThreads * kVec) + uint64_t(threadIdx.x) * kVec;
+      if (e0 >= n) break;
+      float q[kVec];
       for (uint32_t j = 0; j < kVec; ++j) {
-        if (e0 + j >= n) break;
-        const double d = static_cast<double>(__fdiv_rn(grad_at(g, e0 + j), scale));
-        acc = __fma_rn(d, d, acc);  // exact square, one rounding
+        const float u = e0 + j < n ? __fdiv_rn(grad_at(g, e0 + j), scale) : 0.0f;
+        q[j] = __fmul_rn(u, u);
       }
+      const float p = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[1]), __fadd_rn(q[2], q[3])),
+                                __fadd_rn(__fadd_rn(q[4], q[5]), __fadd_rn(q[6], q[7])));
+      acc = __dadd_rn(acc, static_cast<double>(p));
     }
     bad |= !isfinite(acc);
     const double total = fold256(acc, warp_sums);

@@ -10,7 +10,9 @@ namespace slmopt {
 // Fixed reduction tree of the global norm.  A chunk is 65,536 consecutive
 // elements of the flat PARAM-001 buffer; its f64 partial is formed by a
 // 256-thread block in which thread t owns, for k = 0..31, the 8 elements at
-// chunk_base + k*2048 + t*8 (squares added in that order), each warp folds with
+// chunk_base + k*2048 + t*8: their unscaled values are squared in f32, the 8
+// squares summed pairwise in f32 ((q0+q1)+(q2+q3))+((q4+q5)+(q6+q7)), and the
+// sums added in k order to the thread's f64 accumulator; each warp folds with
 // shuffle offsets 16,8,4,2,1 and the 8 warp results fold with offsets 4,2,1.
 // The partials of all chunks are reduced by the same shape (thread t adds
 // partials t, t+256, ... in order).  The shape never depends on the grid, the
@@ -169,6 +171,14 @@ cudaError_t launch_zero1_reduce(int dtype, const void* recv, uint32_t ranks, uin
 cudaError_t launch_zero1_finalize(const double* gathered, uint32_t ranks, uint32_t per_rank,
                                   DeviceScaler* scaler, DeviceStepState* st,
                                   const FinalizeParams& fp, cudaStream_t stream);
+// Micro-batch accumulation (acc = acc + micro, or acc = micro), and the last
+// micro-batch fused with the norm pass over the accumulated values.
+cudaError_t launch_accumulate(int dtype, float* acc, const void* micro, uint64_t n,
+                              int overwrite, cudaStream_t stream);
+cudaError_t launch_accumulate_norm(int dtype, float* acc, const void* micro, uint64_t n,
+                                   int overwrite, uint32_t n_chunks, DeviceScaler* scaler,
+                                   double* partials, DeviceStepState* st,
+                                   const FinalizeParams& fp, cudaStream_t stream);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

@@ -141,6 +141,9 @@ SIGNATURES = [
     ("slm_opt_read_result", _I, [_P, ctypes.POINTER(StepResult)]),
     ("slm_opt_norm_pass", _I, [_P, _P, _I, _I, ctypes.POINTER(StepConfig), _P]),
     ("slm_opt_update_pass", _I, [_P, ctypes.POINTER(StepConfig), _P]),
+    ("slm_grad_accumulate", _I, [_P, _P, _I, _U64, _I, _P]),
+    ("slm_opt_norm_pass_accumulate", _I, [_P, _P, _P, _I, _I, _I, ctypes.POINTER(StepConfig),
+                                          _P]),
     ("slm_opt_apply_update", _I, [_P, _P, _U64, _F, _U64, _U64, ctypes.c_char_p]),
     ("slm_zero1_unique_id", _I, [_P]),
     ("slm_opt_create_zero1", _I, [ctypes.POINTER(TensorSpec), _U32, _I, _I, _I, _P, _U32,

@@ -218,6 +218,29 @@ class B200Adamw:
                                                _stream_handle(stream)))
         return keep
 
+    def accumulate(self, acc, micro, overwrite: bool = False, stream=None) -> None:
+        """acc (device f32[P]) += micro (device f32 or bf16 [P]), or acc = micro."""
+        ptr, dt, mem, n, keep = _grad_pointer(micro)
+        if mem != _lib.MEMORY_DEVICE or not acc.is_cuda:
+            raise ValueError("accumulate works on device tensors")
+        if n != self.P or acc.numel() != self.P:
+            raise ValueError(f"expected {self.P} elements")
+        _lib.check(self.lib.slm_grad_accumulate(acc.data_ptr(), ptr, dt, n, 1 if overwrite else 0,
+                                                _stream_handle(stream)))
+
+    def norm_pass_accumulate(self, acc, micro, options: StepOptions | None = None,
+                             overwrite: bool = False, stream=None):
+        """Last micro-batch: acc += micro fused with the norm pass over acc;
+        follow with update_pass().  Returns the keep-alive for micro."""
+        ptr, dt, mem, n, keep = _grad_pointer(micro)
+        if n != self.P or acc.numel() != self.P:
+            raise ValueError(f"expected {self.P} elements")
+        cfg = (options or StepOptions()).to_c()
+        self._check(self.lib.slm_opt_norm_pass_accumulate(
+            self._h, acc.data_ptr(), ptr, dt, mem, 1 if overwrite else 0, ctypes.byref(cfg),
+            _stream_handle(stream)))
+        return keep
+
     def update_pass(self, options: StepOptions | None = None, stream=None) -> None:
         cfg = (options or StepOptions()).to_c()
         self._check(self.lib.slm_opt_update_pass(self._h, ctypes.byref(cfg),

@@ -119,6 +119,25 @@ class Zero1Adamw(B200Adamw):
 
 
 # ---- multi-GPU benchmark (bench.py --gpus N under torchrun) ----------------------------
+class _stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration of a block."""
+
+    def __enter__(self):
+        import sys
+
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+
+    def __exit__(self, *exc):
+        import sys
+
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
+
 def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> None:
     """ZeRO-1 step on N GPUs: every rank holds its own seeded bf16 gradient
     (seed = rank) x 65,536; value = P / (max over ranks of the step time)."""
@@ -145,7 +164,12 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     P = table.parameter_count
     ids = [unique_id() if rank == 0 else None]
     dist.broadcast_object_list(ids, src=0)
-    opt = Zero1Adamw(table, rank, world, ids[0], device=local, timeout_ms=120000)
+    # Native libraries may print banners on stdout while the communicator is
+    # set up; rank 0's stdout must carry exactly one JSON line.
+    with _stdout_to_stderr():
+        opt = Zero1Adamw(table, rank, world, ids[0], device=local, timeout_ms=120000)
+    if getattr(args, "exchange", "peer") == "nccl":
+        opt.set_exchange(_lib.ZERO1_NCCL)
     state = synth.optimizer_state(P, 0)
     opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
                    validate=False)
@@ -161,9 +185,10 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     opts = StepOptions(learning_rate=3e-4, one_based_update=10,
                        loss_scale_mode=_lib.SCALE_DYNAMIC)
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        opt.step(dev, opts, stream=stream, wait=False)
-    first = opt.read_result()
+    with _stdout_to_stderr():
+        for _ in range(args.warmup):
+            opt.step(dev, opts, stream=stream, wait=False)
+        first = opt.read_result()
     if first.status != 0 or first.skipped:
         raise RuntimeError(f"warm-up step failed on rank {rank}: {first.as_dict()}")
     K = args.steps

@@ -414,3 +414,41 @@ def test_stress_trajectory_bit_exact_and_repeatable(torch):
     assert sum(x[0] for x in res_a) == len(inject)
     for key in state_a:
         assert_same_bits(state_a[key], ost[key], key)
+
+
+# ---- micro-batch accumulation (src/train/trainer.rs:856-904) ------------------------------
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_accumulated_micro_batches_then_fused_norm_and_update(torch, dtype):
+    # Four micro-batch gradient sums accumulated in f32 on the device, the last
+    # one fused with the norm pass, normalised by the update's 65,536 targets;
+    # equal, bit for bit, to the oracle step on the host-accumulated gradient.
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    n = table.parameter_count
+    micro = []
+    for i in range(4):
+        g = (synth.grads_f32(n, 20 + i) * np.float32(16384.0)).astype(np.float32)
+        micro.append(synth.bf16_rne_bits(g) if dtype == "bf16" else g)
+    as_f32 = [synth.bf16_bits_to_f32(m) if dtype == "bf16" else m for m in micro]
+    want_acc = as_f32[0].copy()
+    for m in as_f32[1:]:
+        want_acc = (want_acc + m).astype(np.float32)
+    opts = StepOptions(learning_rate=3e-4, one_based_update=7, static_loss_scale=65536.0)
+    state = synth.optimizer_state(n, 21)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        acc = torch.empty(n, dtype=torch.float32, device="cuda")
+        dev = [to_device(torch, m) for m in micro]
+        opt.accumulate(acc, dev[0], overwrite=True)
+        opt.accumulate(acc, dev[1])
+        opt.accumulate(acc, dev[2])
+        keep = opt.norm_pass_accumulate(acc, dev[3], opts)
+        opt.update_pass(opts)
+        res = opt.read_result()
+        del keep
+        got = opt.read_state()
+        got_acc = acc.cpu().numpy()
+    assert_same_bits(got_acc, want_acc, "accumulator")
+    ost = {k: v.copy() for k, v in state.items()}
+    ores = oracle.step(oracle.make_config(lr=3e-4, t=7, static_scale=65536.0), want_acc,
+                       table.offsets, table.decay, ost, threads=THREADS)
+    check_equal(res, got, ores, ost)

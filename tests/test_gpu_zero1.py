@@ -163,3 +163,112 @@ def test_zero1_equals_single_replica(table_name, exchange):
         assert p["d2"] == p["d1"]
         assert p["r3"]["skipped"] == 1 and p["r3"]["next_loss_scale"] == 16384.0
         assert p["scale"][0] == 16384.0 and p["d3"] == p["d1"]
+
+
+STRESS_STEPS = 100
+STRESS_INJECT = {17: 1, 63: 0}  # step -> rank whose gradient gets an inf
+
+
+def _stress_grads(P: int, table: TensorTable, rank: int, t: int, scale: float) -> np.ndarray:
+    g = synth.grads_student_t(P, 100 + rank, t)
+    bits = synth.bf16_rne_bits((g * np.float32(scale)).astype(np.float32))
+    if STRESS_INJECT.get(t) == rank:
+        synth.inject_nonfinite(bits, t, table.offsets)
+    return bits
+
+
+def _stress_rank(rank, world, port, out_q):
+    try:
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from slmopt import StepOptions, _lib
+        from slmopt.zero1 import Zero1Adamw, unique_id
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=120))
+        table = _table("smoke")
+        P = table.parameter_count
+        runs = []
+        for _ in range(2):  # two full runs must be bit-identical
+            ids = [unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(ids, src=0)
+            opt = Zero1Adamw(table, rank, world, ids[0], device=rank, timeout_ms=120000)
+            st = synth.optimizer_state(P, 0)
+            opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+            opt.set_loss_scale(65536.0)
+            scale, trace = 65536.0, []
+            for t in range(1, STRESS_STEPS + 1):
+                lr = float(np.float32(_lr(t)))
+                r = opt.step(torch.from_numpy(_stress_grads(P, table, rank, t, scale)).cuda(),
+                             StepOptions(learning_rate=lr, one_based_update=t,
+                                         loss_scale_mode=_lib.SCALE_DYNAMIC))
+                trace.append((r.skipped, r.sum_squares, r.clip_scale, r.next_loss_scale))
+                scale = r.next_loss_scale
+            runs.append((trace, _digest(opt.read_state())))
+            opt.close()
+        out_q.put((rank, {"runs": runs}))
+        dist.destroy_process_group()
+    except Exception:
+        out_q.put((rank, {"error": traceback.format_exc()}))
+
+
+def _lr(t: int) -> float:
+    return oracle.schedule_learning_rate(t, 3e-4, 3e-5, 20, 100)[1]
+
+
+def test_zero1_stress_trajectory_matches_oracle():
+    # warmup 20 then cosine from 3e-4 over 100 steps, Student-t(3) * 1e-3 bf16
+    # gradients per rank, dynamic loss scale, +inf injected at two seeded steps
+    n = _gpus()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = min(n, 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_stress_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res, deadline = {}, time.time() + 900
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, payload = q.get(timeout=2.0)
+            res[r] = payload
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert len(res) == world, res
+    for r, p in res.items():
+        assert "error" not in p, p["error"]
+        assert p["runs"][0] == p["runs"][1], f"rank {r}: two runs differ"
+    table = _table("smoke")
+    P = table.parameter_count
+    state = synth.optimizer_state(P, 0)
+    scaler = oracle.Scaler(65536.0, 0)
+    trace = res[0]["runs"][0][0]
+    for t in range(1, STRESS_STEPS + 1):
+        g = oracle.rank_sum_bf16([_stress_grads(P, table, r, t, scaler.scale)
+                                  for r in range(world)], threads=8)
+        ref = oracle.step(oracle.make_config(lr=_lr(t), t=t, dynamic=True), g, table.offsets,
+                          table.decay, state, scaler, threads=8)
+        skipped, s, c, nxt = trace[t - 1]
+        assert skipped == ref.skipped, t
+        if not ref.skipped:
+            assert s == ref.sum_squares and np.float32(c) == np.float32(ref.clip_scale), t
+        assert nxt == ref.next_loss_scale, t
+    assert sum(x[0] for x in trace) == len(STRESS_INJECT)
+    want = _digest(state)
+    for r, p in res.items():
+        assert p["runs"][0][1] == want, f"rank {r} final state differs from the oracle"

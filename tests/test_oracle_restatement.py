@@ -56,16 +56,18 @@ def np_tree_fold(lane: np.ndarray) -> np.float64:
 def np_chunk_partials(g: np.ndarray) -> np.ndarray:
     n = g.size
     c = (n + 65535) // 65536
-    padded = np.zeros(c * 65536, np.float64)
-    padded[:n] = g.astype(np.float64)
-    sq = padded * padded
+    padded = np.zeros(c * 65536, np.float32)
+    padded[:n] = g
+    q = (padded * padded).astype(np.float32)  # f32 squares
     out = np.empty(c, np.float64)
     for ci in range(c):
-        blk = sq[ci * 65536:(ci + 1) * 65536].reshape(32, 256, 8)  # [k][thread][j]
+        blk = q[ci * 65536:(ci + 1) * 65536].reshape(32, 256, 8)  # [k][thread][j]
+        # per-vector pairwise f32 sum ((q0+q1)+(q2+q3))+((q4+q5)+(q6+q7))
+        p = ((blk[:, :, 0] + blk[:, :, 1]) + (blk[:, :, 2] + blk[:, :, 3])) + \
+            ((blk[:, :, 4] + blk[:, :, 5]) + (blk[:, :, 6] + blk[:, :, 7]))
         acc = np.zeros(256, np.float64)
         for k in range(32):
-            for j in range(8):
-                acc = acc + blk[k, :, j]
+            acc = acc + p[k].astype(np.float64)
         out[ci] = np_tree_fold(acc)
     return out
 
@@ -138,9 +140,9 @@ def test_chunk_tree_matches_numpy(n):
     assert np.array_equal(p_c.view(np.uint64), p_np.view(np.uint64))
     assert not flags.any()
     assert oracle.tree_sum(p_c) == np_tree_sum(p_np)
-    # the fixed tree agrees with an exact-ish sequential sum far below 1e-6
+    # the fixed tree agrees with the exact sum far inside 1e-6 relative
     exact = math.fsum(float(x) * float(x) for x in g.astype(np.float64))
-    assert abs(oracle.tree_sum(p_c) - exact) <= 1e-12 * max(exact, 1e-300)
+    assert abs(oracle.tree_sum(p_c) - exact) <= 3e-7 * max(exact, 1e-300)
 
 
 def test_tree_sum_is_invariant_to_zero_padding():

@@ -1001,40 +1001,58 @@ __global__ void peer_barrier_kernel(PeerTable pt, int rank, int world, uint32_t 
 // 0..N-1, unscaled and reduced to chunk partials exactly like a single
 // replica.  The last block pushes this rank's partials and non-finite flag
 // into every rank's gathered area and raises their partials flag.
-template <typename GT, bool kMul>
+template <typename GT, bool kMul, int kBatch, int kRanks>
 __device__ __forceinline__ double p2p_thread_sum(const PeerTable& pt, int world,
                                                  uint64_t shard_begin, uint64_t base,
                                                  uint64_t n, float* __restrict__ gsum,
                                                  const ScaleInfo& sc) {
   double acc = 0.0;
+  if (base + kChunkElems <= n) {
+    // Whole chunk: kBatch vectors of every rank (kBatch * kRanks 16/32-byte
+    // loads, mostly over NVLink) go out before any is added.
+#pragma unroll 1
+    for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kBatch) {
+      RawVec<GT> raw[kBatch][kRanks];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const uint64_t e0 = base + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec) +
+                            static_cast<uint64_t>(threadIdx.x) * kVec;
+#pragma unroll
+        for (int q = 0; q < kRanks; ++q)
+          if (q < world) raw[b][q].load(static_cast<const GT*>(pt.grads[q]) + shard_begin + e0);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const uint64_t e0 = base + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec) +
+                            static_cast<uint64_t>(threadIdx.x) * kVec;
+        float s[kVec];
+        raw[b][0].unpack(s);
+#pragma unroll
+        for (int q = 1; q < kRanks; ++q)
+          if (q < world) {
+            float x[kVec];
+            raw[b][q].unpack(x);
+#pragma unroll
+            for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
+          }
+        __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
+        __stcg(reinterpret_cast<float4*>(gsum + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
+        acc = add_squares8<kMul>(acc, s, sc);
+      }
+    }
+    return acc;
+  }
   for (uint32_t k = 0; k < kChunkIters; ++k) {
     const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
                         static_cast<uint64_t>(threadIdx.x) * kVec;
     if (e0 >= n) break;
     float s[kVec];
-    if (e0 + kVec <= n) {
-      // Every rank's 16/32 bytes go out before any is added (packed meanwhile).
-      RawVec<GT> raw[kMaxRanks];
+    load_grad8(static_cast<const GT*>(pt.grads[0]) + shard_begin, e0, n, s);
+    for (int q = 1; q < world; ++q) {
+      float x[kVec];
+      load_grad8(static_cast<const GT*>(pt.grads[q]) + shard_begin, e0, n, x);
 #pragma unroll
-      for (int q = 0; q < kMaxRanks; ++q)
-        if (q < world) raw[q].load(static_cast<const GT*>(pt.grads[q]) + shard_begin + e0);
-      raw[0].unpack(s);
-#pragma unroll
-      for (int q = 1; q < kMaxRanks; ++q)
-        if (q < world) {
-          float x[kVec];
-          raw[q].unpack(x);
-#pragma unroll
-          for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
-        }
-    } else {
-      load_grad8(static_cast<const GT*>(pt.grads[0]) + shard_begin, e0, n, s);
-      for (int q = 1; q < world; ++q) {
-        float x[kVec];
-        load_grad8(static_cast<const GT*>(pt.grads[q]) + shard_begin, e0, n, x);
-#pragma unroll
-        for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
-      }
+      for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
     }
     if (e0 + kVec <= n) {
       __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
@@ -1047,7 +1065,7 @@ __device__ __forceinline__ double p2p_thread_sum(const PeerTable& pt, int world,
   return acc;
 }
 
-template <typename GT>
+template <typename GT, int kBatch, int kRanks>
 __global__ void __launch_bounds__(kTreeThreads)
     zero1_p2p_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
                             uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
@@ -1061,8 +1079,11 @@ __global__ void __launch_bounds__(kTreeThreads)
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
     const double acc =
-        sc.mul ? p2p_thread_sum<GT, true>(pt, world, shard_begin, base, n_valid, gsum, sc)
-               : p2p_thread_sum<GT, false>(pt, world, shard_begin, base, n_valid, gsum, sc);
+        sc.mul
+            ? p2p_thread_sum<GT, true, kBatch, kRanks>(pt, world, shard_begin, base, n_valid,
+                                                       gsum, sc)
+            : p2p_thread_sum<GT, false, kBatch, kRanks>(pt, world, shard_begin, base, n_valid,
+                                                        gsum, sc);
     bad |= !isfinite(acc);
     const double total = block_fold(acc, warp_sums);
     if (threadIdx.x == 0) send[c] = total;
@@ -1284,12 +1305,20 @@ cudaError_t launch_zero1_p2p_reduce(int dtype, const PeerTable& pt, int rank, in
                                     float* gsum, double* send, uint32_t epoch,
                                     DeviceStepState* st, cudaStream_t stream) {
   if (n_chunks == 0) return cudaErrorInvalidValue;
-  if (dtype == 0)
-    zero1_p2p_reduce_kernel<float><<<n_chunks, kTreeThreads, 0, stream>>>(
-        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st);
-  else
-    zero1_p2p_reduce_kernel<uint16_t><<<n_chunks, kTreeThreads, 0, stream>>>(
-        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st);
+  // Loads in flight per thread: kBatch vectors x up to kRanks ranks (8 per batch).
+#define SLM_P2P_LAUNCH(GT, B, R)                                                          \
+  zero1_p2p_reduce_kernel<GT, B, R><<<n_chunks, kTreeThreads, 0, stream>>>(              \
+      pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st)
+  if (dtype == 0) {
+    if (world <= 2) SLM_P2P_LAUNCH(float, 4, 2);
+    else if (world <= 4) SLM_P2P_LAUNCH(float, 2, 4);
+    else SLM_P2P_LAUNCH(float, 1, 8);
+  } else {
+    if (world <= 2) SLM_P2P_LAUNCH(uint16_t, 4, 2);
+    else if (world <= 4) SLM_P2P_LAUNCH(uint16_t, 2, 4);
+    else SLM_P2P_LAUNCH(uint16_t, 1, 8);
+  }
+#undef SLM_P2P_LAUNCH
   return cudaGetLastError();
 }
 

@@ -227,7 +227,7 @@ struct PartialsView {
 // Reduce the partials with the fixed tree, decide clip / skip, advance the
 // scaler.  Called by one whole 256-thread block; `nonfinite` is read from
 // thread 0 only.
-__device__ void finalize_block(const PartialsView& partials, uint32_t nonfinite,
+__device__ __forceinline__ void finalize_block(const PartialsView& partials, uint32_t nonfinite,
                                DeviceStepState* st, DeviceScaler* scaler,
                                const FinalizeParams& fp, double* warp_sums) {
   double v = 0.0;
@@ -384,11 +384,10 @@ __global__ void __launch_bounds__(256)
 // by the thread that owns it in the fixed tree, which then adds the square of
 // the unscaled sum -- the same partials norm_partials_kernel<float> would form
 // from the finished accumulator, without reading it again.
-template <typename GT, bool kMul>
+template <typename GT, bool kMul, bool kOverwrite>
 __device__ __forceinline__ double accum_thread_sum(float* __restrict__ acc,
                                                    const GT* __restrict__ micro, uint64_t base,
-                                                   uint64_t n, bool overwrite,
-                                                   const ScaleInfo& sc) {
+                                                   uint64_t n, const ScaleInfo& sc) {
   double a = 0.0;
 #pragma unroll 2
   for (uint32_t k = 0; k < kChunkIters; ++k) {
@@ -396,7 +395,7 @@ __device__ __forceinline__ double accum_thread_sum(float* __restrict__ acc,
                         static_cast<uint64_t>(threadIdx.x) * kVec;
     if (e0 >= n) break;
     float s[kVec];
-    accumulate8(acc, micro, e0, n, overwrite, s);
+    accumulate8(acc, micro, e0, n, kOverwrite, s);
     a = add_squares8<kMul>(a, s, sc);
   }
   return a;
@@ -414,8 +413,11 @@ __global__ void __launch_bounds__(kTreeThreads)
   bool bad = false;
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
-    const double a = sc.mul ? accum_thread_sum<GT, true>(acc, micro, base, n, overwrite, sc)
-                            : accum_thread_sum<GT, false>(acc, micro, base, n, overwrite, sc);
+    const double a =
+        overwrite ? (sc.mul ? accum_thread_sum<GT, true, true>(acc, micro, base, n, sc)
+                            : accum_thread_sum<GT, false, true>(acc, micro, base, n, sc))
+                  : (sc.mul ? accum_thread_sum<GT, true, false>(acc, micro, base, n, sc)
+                            : accum_thread_sum<GT, false, false>(acc, micro, base, n, sc));
     bad |= !isfinite(a);
     const double total = block_fold(a, warp_sums);
     if (threadIdx.x == 0) partials[c] = total;
@@ -544,38 +546,19 @@ __device__ __forceinline__ void ld8_stream(const float* __restrict__ p, float (&
   x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
 }
 
-__device__ __forceinline__ void st8_stream(float* __restrict__ p, const float (&x)[8]) {
+[[maybe_unused]] __device__ __forceinline__ void st8_stream(float* __restrict__ p, const float (&x)[8]) {
   __stcs(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
   __stcs(reinterpret_cast<float4*>(p + 4), make_float4(x[4], x[5], x[6], x[7]));
 }
 
-__device__ __forceinline__ void ld_grad8_stream(const float* __restrict__ g, float (&x)[8]) {
+[[maybe_unused]] __device__ __forceinline__ void ld_grad8_stream(const float* __restrict__ g, float (&x)[8]) {
   ld8_stream(g, x);
 }
 
-__device__ __forceinline__ void ld_grad8_stream(const uint16_t* __restrict__ g, float (&x)[8]) {
+[[maybe_unused]] __device__ __forceinline__ void ld_grad8_stream(const uint16_t* __restrict__ g, float (&x)[8]) {
   unpack_bf16x8(__ldcs(reinterpret_cast<const uint4*>(g)), x);
 }
 
-
-// Bulk prefetch of [p, p + bytes) into L2 (no registers, no shared memory):
-// keeps the next tile's bytes in flight while this tile computes.  p and bytes
-// must be multiples of 16.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-template <typename GT>
-__device__ __forceinline__ void prefetch_tile(uint64_t tile, uint64_t n, const GT* g,
-                                              const float* master, const float* mom,
-                                              const float* var) {
-  const uint64_t e0 = tile * kTileElems;
-  if (e0 + kTileElems > n) return;  // only whole tiles (16-byte multiples)
-  prefetch_l2(g + e0, kTileElems * sizeof(GT));
-  prefetch_l2(master + e0, kTileElems * 4);
-  prefetch_l2(mom + e0, kTileElems * 4);
-  prefetch_l2(var + e0, kTileElems * 4);
-}
 
 // Decay weight of global element e, scanning forward from tensor k.
 __device__ __forceinline__ float decay_of(uint64_t e, uint32_t& k,
@@ -598,16 +581,7 @@ __device__ __forceinline__ bool update_loop(const GT* __restrict__ g, uint64_t n
                                             float clip, const PeerStores& ps) {
   bool bad = false;
   const uint64_t n_tiles = (n + kTileElems - 1) / kTileElems;
-  if constexpr (kUpdatePrefetch > 0) {
-    if (threadIdx.x == 0)
-      for (uint32_t d = 1; d < kUpdatePrefetch; ++d)
-        prefetch_tile(blockIdx.x + uint64_t(d) * gridDim.x, n, g, master, mom, var);
-  }
   for (uint64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-    if constexpr (kUpdatePrefetch > 0) {
-      if (threadIdx.x == 0)
-        prefetch_tile(tile + uint64_t(kUpdatePrefetch) * gridDim.x, n, g, master, mom, var);
-    }
     const uint32_t first = __ldg(tile_first + tile);
     uint64_t i0[kUpdateUnroll];
     bool full[kUpdateUnroll];
@@ -775,9 +749,53 @@ struct BulkStage {
   static constexpr uint32_t kBytes = kG + 3 * kF;
 };
 
-template <typename GT>
+// Shared memory: kBulkStages stages, the full/empty mbarriers (one 128-byte
+// slot), and on the peer path two bf16 staging tiles for the weight stores.
+constexpr uint32_t kBarrierBytes = 128;
+static_assert(2 * kBulkStages * sizeof(uint64_t) <= kBarrierBytes, "mbarrier slot too small");
+constexpr uint32_t kStagingBytes = kBulkTile * 2;
+
+template <typename GT, bool kPeers>
 constexpr size_t bulk_smem_bytes() {
-  return size_t(kBulkStages) * BulkStage<GT>::kBytes + 2 * kBulkStages * sizeof(uint64_t);
+  return size_t(kBulkStages) * BulkStage<GT>::kBytes + kBarrierBytes +
+         (kPeers ? 2 * kStagingBytes : 0);
+}
+
+// Bulk (TMA engine) store of `bytes` from shared to global memory, tracked in
+// this thread's bulk async-group; dst, src and bytes are multiples of 16.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Every committed group of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every committed group of this thread has completed its writes.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Generic-proxy writes to shared memory become visible to the bulk engine.
+__device__ __forceinline__ void fence_smem_to_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// AND of `ok` over the 256 consumer threads (named barrier 1; the producer
+// warp never takes part).
+__device__ __forceinline__ bool consumers_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u), "n"(kBulkConsumers)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ void lds4(const float* p, float (&x)[4]) {
@@ -795,16 +813,17 @@ __device__ __forceinline__ void lds_grad4(const uint16_t* p, float (&x)[4]) {
 }
 
 // AdamW on 4 consecutive local elements starting at i (global elem_base + i)
-// whose g / master / m / v are already in registers; streams the results out.
-template <bool kMul, bool kPeers>
-__device__ __forceinline__ void update4(uint64_t i, uint64_t elem_base, float (&gx)[4],
+// whose g / master / m / v are already in registers; streams master / m / v
+// out and returns the 4 bf16 weights packed.
+template <bool kMul>
+__device__ __forceinline__ uint2 update4(uint64_t i, uint64_t elem_base, float (&gx)[4],
                                         float (&th)[4], float (&mm)[4], float (&vv)[4],
                                         float* __restrict__ master, float* __restrict__ mom,
-                                        float* __restrict__ var, uint16_t* __restrict__ w16,
+                                        float* __restrict__ var,
                                         const uint64_t* __restrict__ offsets,
                                         const uint8_t* __restrict__ decay, uint32_t k,
                                         const AdamwParams& p, const ScaleInfo& sc, float clip,
-                                        const PeerStores& ps, bool& bad) {
+                                        bool& bad) {
   const uint64_t e0 = elem_base + i;
   const float wd0 = decay_of(e0, k, offsets, decay, p);
   const bool uniform = e0 + 4 <= __ldg(offsets + k + 1);
@@ -819,21 +838,22 @@ __device__ __forceinline__ void update4(uint64_t i, uint64_t elem_base, float (&
   __stcs(reinterpret_cast<float4*>(master + i), make_float4(th[0], th[1], th[2], th[3]));
   __stcs(reinterpret_cast<float4*>(mom + i), make_float4(mm[0], mm[1], mm[2], mm[3]));
   __stcs(reinterpret_cast<float4*>(var + i), make_float4(vv[0], vv[1], vv[2], vv[3]));
-  const uint2 packed = make_uint2(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16));
-  __stcs(reinterpret_cast<uint2*>(w16 + i), packed);
-  if constexpr (kPeers) {
-#pragma unroll
-    for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
-      if (q < ps.count) __stcs(reinterpret_cast<uint2*>(ps.w16[q] + i), packed);
-  }
+  return make_uint2(bits[0] | (bits[1] << 16), bits[2] | (bits[3] << 16));
 }
 
+// Peer path (kPeers): the tile's bf16 weights go through a shared-memory
+// staging tile and leave as one 4 KB bulk store per destination (this rank's
+// copy and every peer's), issued by consumer thread 0, so the consumer warps
+// never wait on NVLink stores.  Staging tile i % 2 is rewritten two tiles
+// later; thread 0 waits for every earlier store group to finish reading before
+// the consumers' barrier of the tile in between, which makes that safe.  The
+// barrier also ANDs the threads' wait outcomes so that all 256 leave together.
 template <typename GT, bool kMul, bool kPeers>
 __device__ __forceinline__ bool bulk_consume(uint8_t* smem, uint64_t* full_bar,
-                                             uint64_t* empty_bar, uint64_t n_full,
-                                             uint64_t elem_base, float* __restrict__ master,
-                                             float* __restrict__ mom, float* __restrict__ var,
-                                             uint16_t* __restrict__ w16,
+                                             uint64_t* empty_bar, uint8_t* staging,
+                                             uint64_t n_full, uint64_t elem_base,
+                                             float* __restrict__ master, float* __restrict__ mom,
+                                             float* __restrict__ var, uint16_t* __restrict__ w16,
                                              const uint64_t* __restrict__ offsets,
                                              const uint8_t* __restrict__ decay,
                                              const uint32_t* __restrict__ tile_first,
@@ -844,27 +864,49 @@ __device__ __forceinline__ bool bulk_consume(uint8_t* smem, uint64_t* full_bar,
   uint32_t i = 0;
   for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
     const uint32_t s = i % kBulkStages;
-    if (!mbar_wait(&full_bar[s], (i / kBulkStages) & 1u)) return false;
-    const uint8_t* base = smem + size_t(s) * Stage::kBytes;
-    const GT* sg = reinterpret_cast<const GT*>(base);
-    const float* sm = reinterpret_cast<const float*>(base + Stage::kG);
-    const float* s1 = sm + kBulkTile;
-    const float* s2 = s1 + kBulkTile;
-    const uint64_t tile0 = tile * kBulkTile;
-    const uint32_t k = __ldg(tile_first + tile0 / kTileElems);
-#pragma unroll
-    for (uint32_t h = 0; h < 2; ++h) {
-      const uint32_t o = h * (kBulkTile / 2) + 4 * t;
-      float gx[4], th[4], mm[4], vv[4];
-      lds_grad4(sg + o, gx);
-      lds4(sm + o, th);
-      lds4(s1 + o, mm);
-      lds4(s2 + o, vv);
-      update4<kMul, kPeers>(tile0 + o, elem_base, gx, th, mm, vv, master, mom, var, w16, offsets, decay,
-                    k, p, sc, clip, ps, bad);
+    const bool ready = mbar_wait(&full_bar[s], (i / kBulkStages) & 1u);
+    if constexpr (!kPeers) {
+      if (!ready) return false;
     }
-    __syncwarp();
-    if ((t & 31) == 0) mbar_arrive(&empty_bar[s]);
+    const uint64_t tile0 = tile * kBulkTile;
+    uint16_t* stage_w16 = reinterpret_cast<uint16_t*>(staging + (i & 1u) * kStagingBytes);
+    if (ready) {
+      const uint8_t* base = smem + size_t(s) * Stage::kBytes;
+      const GT* sg = reinterpret_cast<const GT*>(base);
+      const float* sm = reinterpret_cast<const float*>(base + Stage::kG);
+      const float* s1 = sm + kBulkTile;
+      const float* s2 = s1 + kBulkTile;
+      const uint32_t k = __ldg(tile_first + tile0 / kTileElems);
+#pragma unroll
+      for (uint32_t h = 0; h < 2; ++h) {
+        const uint32_t o = h * (kBulkTile / 2) + 4 * t;
+        float gx[4], th[4], mm[4], vv[4];
+        lds_grad4(sg + o, gx);
+        lds4(sm + o, th);
+        lds4(s1 + o, mm);
+        lds4(s2 + o, vv);
+        const uint2 packed = update4<kMul>(tile0 + o, elem_base, gx, th, mm, vv, master, mom,
+                                           var, offsets, decay, k, p, sc, clip, bad);
+        if constexpr (kPeers)
+          *reinterpret_cast<uint2*>(stage_w16 + o) = packed;
+        else
+          __stcs(reinterpret_cast<uint2*>(w16 + tile0 + o), packed);
+      }
+      __syncwarp();
+      if ((t & 31) == 0) mbar_arrive(&empty_bar[s]);
+    }
+    if constexpr (kPeers) {
+      fence_smem_to_async();
+      if (t == 0) bulk_wait_read_all();  // staging tile (i + 1) % 2 is free again
+      if (!consumers_all(ready)) return false;
+      if (t == 0) {
+        bulk_store(w16 + tile0, stage_w16, kStagingBytes);
+#pragma unroll
+        for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+          if (q < ps.count) bulk_store(ps.w16[q] + tile0, stage_w16, kStagingBytes);
+        bulk_commit();
+      }
+    }
   }
   return true;
 }
@@ -883,6 +925,7 @@ __global__ void __launch_bounds__(kBulkThreads)
   if (st->skipped || st->kernel_error) return;  // uniform for the grid
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(kBulkStages) * Stage::kBytes);
   uint64_t* empty_bar = full_bar + kBulkStages;
+  uint8_t* staging = smem + size_t(kBulkStages) * Stage::kBytes + kBarrierBytes;
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kBulkStages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -916,12 +959,20 @@ __global__ void __launch_bounds__(kBulkThreads)
       }
     }
   } else {
-    ok = sc.mul ? bulk_consume<GT, true, kPeers>(smem, full_bar, empty_bar, n_full, elem_base, master,
-                                         mom, var, w16, offsets, decay, tile_first, p, sc, clip,
-                                         ps, bad)
-                : bulk_consume<GT, false, kPeers>(smem, full_bar, empty_bar, n_full, elem_base, master,
-                                          mom, var, w16, offsets, decay, tile_first, p, sc, clip,
-                                          ps, bad);
+    ok = sc.mul ? bulk_consume<GT, true, kPeers>(smem, full_bar, empty_bar, staging, n_full,
+                                                 elem_base, master, mom, var, w16, offsets, decay,
+                                                 tile_first, p, sc, clip, ps, bad)
+                : bulk_consume<GT, false, kPeers>(smem, full_bar, empty_bar, staging, n_full,
+                                                  elem_base, master, mom, var, w16, offsets,
+                                                  decay, tile_first, p, sc, clip, ps, bad);
+    if constexpr (kPeers) {
+      if (threadIdx.x == 0) {
+        // The bulk stores finish (and release shared memory) before the
+        // block exits and before the closing barrier publishes them.
+        bulk_wait_all();
+        asm volatile("fence.proxy.async;" ::: "memory");
+      }
+    }
     // Ragged tail after the last whole tile: element by element, block 0.
     if (blockIdx.x == 0) {
       for (uint64_t i = n_full * kBulkTile + threadIdx.x; i < n; i += kBulkConsumers) {
@@ -1174,7 +1225,8 @@ namespace {
 template <typename GT, bool kPeers>
 void allow_bulk_smem() {
   cudaFuncSetAttribute(adamw_update_bulk_kernel<GT, kPeers>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(bulk_smem_bytes<GT>()));
+                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(bulk_smem_bytes<GT, kPeers>()));
 }
 
 template <typename GT>
@@ -1185,7 +1237,8 @@ int update_blocks_per_sm() {
     allow_bulk_smem<GT, false>();
     allow_bulk_smem<GT, true>();
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, adamw_update_bulk_kernel<GT, false>, kBulkThreads, bulk_smem_bytes<GT>());
+        &per_sm, adamw_update_bulk_kernel<GT, false>, kBulkThreads,
+        bulk_smem_bytes<GT, false>());
   } else {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_update_kernel<GT, false>,
                                                       kUpdateThreads, 0);
@@ -1204,7 +1257,8 @@ void launch_update_typed(const void* grads, uint64_t n, uint64_t elem_base, floa
     const uint64_t tiles = n / kBulkTile;
     const unsigned blocks =
         static_cast<unsigned>(tiles == 0 ? 1 : (uint64_t(grid) < tiles ? uint64_t(grid) : tiles));
-    adamw_update_bulk_kernel<GT, kPeers><<<blocks, kBulkThreads, bulk_smem_bytes<GT>(), stream>>>(
+    adamw_update_bulk_kernel<GT, kPeers>
+        <<<blocks, kBulkThreads, bulk_smem_bytes<GT, kPeers>(), stream>>>(
         g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st, ps);
   } else {
     const uint64_t tiles = (n + kTileElems - 1) / kTileElems;

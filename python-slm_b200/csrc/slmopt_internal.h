@@ -26,21 +26,16 @@ constexpr uint32_t kChunkIters = kChunkElems / (kTreeThreads * kVec);  // 32
 
 // Update kernel tiling: one 256-thread block step covers kTileElems elements
 // (kUpdateUnroll 8-element vectors per thread).  The build may override the
-// unroll, the minimum resident blocks per SM (register cap) and how many of
-// its own tiles ahead a block bulk-prefetches into L2.
+// unroll and the minimum resident blocks per SM (register cap).
 #ifndef SLM_UPDATE_UNROLL
 #define SLM_UPDATE_UNROLL 2
 #endif
 #ifndef SLM_UPDATE_MIN_BLOCKS
 #define SLM_UPDATE_MIN_BLOCKS 1
 #endif
-#ifndef SLM_UPDATE_PREFETCH
-#define SLM_UPDATE_PREFETCH 0
-#endif
 constexpr uint32_t kUpdateThreads = 256;
 constexpr uint32_t kUpdateUnroll = SLM_UPDATE_UNROLL;
 constexpr uint32_t kUpdateMinBlocks = SLM_UPDATE_MIN_BLOCKS;
-constexpr uint32_t kUpdatePrefetch = SLM_UPDATE_PREFETCH;
 constexpr uint32_t kTileElems = kUpdateThreads * kVec * kUpdateUnroll;
 // Bulk-copy update kernel (SLM_UPDATE_BULK=1): a producer warp streams
 // 2,048-element tiles of g / master / m / v into a ring of shared-memory stages

@@ -182,6 +182,25 @@ int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
 /* Wait for the handle's last enqueued step on its stream and return its result. */
 int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out);
 
+/* Per-phase device timing of slm_opt_step (diagnostics; no counterpart in the
+ * reference, whose step is one host loop).  While enabled, every step records
+ * CUDA events on its stream at its phase boundaries, and the next step first
+ * waits for the previous one to fold its intervals into running sums, so
+ * steps no longer overlap the host: keep it off in timed runs.  Enabling
+ * (again) clears the sums.  slm_opt_phase_times writes up to `capacity` mean
+ * phase durations in ms, the phase count and the number of steps timed;
+ * slm_opt_phase_name names phase i for this handle's mode (NULL past the end):
+ *   one GPU:         norm pass, update
+ *   ZeRO-1 peer:     gradient barrier, peer reduce, finalize,
+ *                    update + weight stores, weight barrier
+ *   ZeRO-1 NCCL:     gradient all-to-all, reduce, partials all-gather,
+ *                    finalize, update, weight all-gather
+ * A host gradient's upload is not part of any phase. */
+int slm_opt_phase_timing(slm_opt_handle* h, int enable);
+int slm_opt_phase_times(slm_opt_handle* h, double* mean_ms, uint32_t capacity,
+                        uint32_t* n_phases, uint64_t* steps);
+const char* slm_opt_phase_name(const slm_opt_handle* h, uint32_t phase);
+
 /* slm_opt_step split in its two device passes, both enqueue-only:
  *   slm_opt_norm_pass   -- stage (host) gradients, unscale, non-finite check,
  *                          fixed-tree norm, clip / skip decision, scaler update

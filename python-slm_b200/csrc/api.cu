@@ -269,6 +269,25 @@ int enqueue_update(slm_opt_handle* h, const void* dev_grads, int dtype,
                  "update kernel");
 }
 
+// Folds the last complete step's phase intervals into the sums (waits for it).
+int phase_harvest(slm_opt_handle* h) {
+  PhaseTimer& t = h->timer;
+  const int n = t.finished;
+  t.finished = 0;
+  if (n < 2) return SLM_OK;
+  int st = h->cuda(cudaEventSynchronize(t.ev[n - 1]), "phase timing");
+  if (st) return st;
+  for (int i = 0; i + 1 < n; ++i) {
+    float ms = 0.0f;
+    if ((st = h->cuda(cudaEventElapsedTime(&ms, t.ev[i], t.ev[i + 1]), "phase timing")))
+      return st;
+    t.acc[i] += ms;
+  }
+  t.phases = uint32_t(n - 1);
+  ++t.steps;
+  return SLM_OK;
+}
+
 int finish_result(slm_opt_handle* h, const DeviceStepState& ds, slm_step_result* out) {
   fill_result(ds, out);
   if (ds.kernel_error) h->broken = true;  // the ranks may be out of step: re-create the handle
@@ -293,6 +312,27 @@ int download_role(slm_opt_handle* h, int role, void* dst, uint64_t bytes) {
 }
 
 }  // namespace
+
+int slmopt::phase_begin(slm_opt_handle* h, cudaStream_t s) {
+  PhaseTimer& t = h->timer;
+  if (!t.enabled) return SLM_OK;
+  t.marks = 0;  // drops the events of a step that failed part-way
+  if (int st = phase_harvest(h)) return st;
+  return phase_mark(h, s);
+}
+
+int slmopt::phase_mark(slm_opt_handle* h, cudaStream_t s) {
+  PhaseTimer& t = h->timer;
+  if (!t.enabled || t.marks >= PhaseTimer::kMaxMarks) return SLM_OK;
+  return h->cuda(cudaEventRecord(t.ev[t.marks++], s), "phase timing");
+}
+
+void slmopt::phase_end(slm_opt_handle* h) {
+  PhaseTimer& t = h->timer;
+  if (!t.enabled) return;
+  t.finished = t.marks;
+  t.marks = 0;
+}
 
 extern "C" {
 
@@ -418,6 +458,8 @@ int slm_opt_destroy(slm_opt_handle* h) {
   if (!h) return SLM_OK;
   DeviceGuard guard(h->device);
   zero1_release(h);
+  if (h->timer.created)
+    for (cudaEvent_t e : h->timer.ev) cudaEventDestroy(e);
   cudaFree(h->master);
   cudaFree(h->m1);
   cudaFree(h->m2);
@@ -632,9 +674,13 @@ int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
   } else {
     const void* dev = nullptr;
     if ((st = stage_grads(h, grads, dtype, memory, s, &dev))) return st;
+    if ((st = phase_begin(h, s))) return st;
     if ((st = enqueue_norm(h, dev, dtype, cfg, s))) return st;
+    if ((st = phase_mark(h, s))) return st;
     if ((st = enqueue_update(h, dev, dtype, cfg, s))) return st;
+    if ((st = phase_mark(h, s))) return st;
   }
+  phase_end(h);
   h->pending = true;
   h->pending_stream = s;
   if (!out) return SLM_OK;
@@ -652,6 +698,55 @@ int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out) {
   if (st) return st;
   h->pending = false;
   return finish_result(h, ds, out);
+}
+
+int slm_opt_phase_timing(slm_opt_handle* h, int enable) {
+  if (!h) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL handle");
+  DeviceGuard guard(h->device);
+  PhaseTimer& t = h->timer;
+  if (enable && !t.created) {
+    for (int i = 0; i < PhaseTimer::kMaxMarks; ++i) {
+      const int st = h->cuda(cudaEventCreate(&t.ev[i]), "cudaEventCreate");
+      if (st) {
+        for (int j = 0; j < i; ++j) cudaEventDestroy(t.ev[j]);
+        return st;
+      }
+    }
+    t.created = true;
+  }
+  t.enabled = enable != 0;
+  t.marks = 0;
+  t.finished = 0;
+  t.steps = 0;
+  t.phases = 0;
+  for (double& a : t.acc) a = 0.0;
+  return SLM_OK;
+}
+
+int slm_opt_phase_times(slm_opt_handle* h, double* mean_ms, uint32_t capacity,
+                        uint32_t* n_phases, uint64_t* steps) {
+  if (!h || !n_phases || !steps || (capacity && !mean_ms))
+    return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  DeviceGuard guard(h->device);
+  if (int st = phase_harvest(h)) return st;
+  const PhaseTimer& t = h->timer;
+  *n_phases = t.phases;
+  *steps = t.steps;
+  for (uint32_t i = 0; i < capacity && i < t.phases; ++i)
+    mean_ms[i] = t.steps ? t.acc[i] / double(t.steps) : 0.0;
+  return SLM_OK;
+}
+
+const char* slm_opt_phase_name(const slm_opt_handle* h, uint32_t phase) {
+  static const char* const kSingle[] = {"norm pass", "update"};
+  static const char* const kPeer[] = {"gradient barrier", "peer reduce", "finalize",
+                                      "update + weight stores", "weight barrier"};
+  static const char* const kNccl[] = {"gradient all-to-all", "reduce", "partials all-gather",
+                                      "finalize", "update", "weight all-gather"};
+  if (!h) return nullptr;
+  if (!h->sharded()) return phase < 2 ? kSingle[phase] : nullptr;
+  if (h->exchange == SLM_ZERO1_PEER) return phase < 5 ? kPeer[phase] : nullptr;
+  return phase < 6 ? kNccl[phase] : nullptr;
 }
 
 int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,

@@ -49,6 +49,22 @@ AdamwParams adamw_params(const slm_step_config* cfg);
 
 }  // namespace slmopt
 
+namespace slmopt {
+// Optional device timing of each slm_opt_step by phase (slm_opt_phase_timing):
+// CUDA events recorded on the step's stream at the phase boundaries.
+struct PhaseTimer {
+  static constexpr int kMaxMarks = 8;
+  bool enabled = false;
+  bool created = false;
+  cudaEvent_t ev[kMaxMarks] = {};
+  int marks = 0;     // events recorded so far for the step being enqueued
+  int finished = 0;  // events of the last complete step, not yet folded into acc
+  double acc[kMaxMarks - 1] = {};
+  uint64_t steps = 0;
+  uint32_t phases = 0;
+};
+}  // namespace slmopt
+
 struct slm_opt_handle {
   int device = 0;
   uint64_t P = 0;  // global parameter count
@@ -104,6 +120,7 @@ struct slm_opt_handle {
   slmopt::PeerTable peers{};       // every rank's buffers as mapped here (own included)
   void* opened[slmopt::kMaxRanks][4] = {};  // IPC mappings to close on destroy
   uint32_t epoch = 0;              // step counter shared (implicitly) by all ranks
+  slmopt::PhaseTimer timer;
 
   bool sharded() const { return world > 1; }
 
@@ -119,6 +136,12 @@ struct slm_opt_handle {
 };
 
 namespace slmopt {
+// Phase timing: phase_begin starts a step (after folding in the previous
+// complete one, which waits for it), phase_mark closes a phase, phase_end
+// marks the step complete.  No-ops unless timing is enabled.
+int phase_begin(slm_opt_handle* h, cudaStream_t s);
+int phase_mark(slm_opt_handle* h, cudaStream_t s);
+void phase_end(slm_opt_handle* h);
 // Allocates the per-handle device state for [shard_begin, shard_begin+shard_len)
 // with the bf16 buffer sized w16_elems; used by both create paths (api.cu).
 int allocate_state(slm_opt_handle* h, uint64_t w16_elems);

@@ -274,19 +274,23 @@ int peer_step(slm_opt_handle* h, const void* dev, int dtype, const slm_step_conf
   const FinalizeParams fp = finalize_params(h, cfg);
   int st;
   (void)dev;
+  if ((st = phase_begin(h, s))) return st;
   if ((st = h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotGrads, epoch,
                                         h->d_state, tmo, s),
                     "gradient barrier")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   if ((st = h->cuda(launch_zero1_p2p_reduce(dtype, h->peers, h->rank, h->world, h->shard_begin,
                                             h->shard_len, h->chunks_per_rank, h->d_scaler, fp,
                                             h->d_gsum, h->d_send, epoch, h->d_state, s),
                     "peer reduce kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   if ((st = h->cuda(launch_zero1_p2p_finalize(h->peers, h->rank, h->world, h->chunks_per_rank,
                                               epoch, h->d_scaler, h->d_state, fp, tmo, s),
                     "peer finalize kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   PeerStores ps{};
   for (int q = 0; q < h->world; ++q)
     if (q != h->rank) ps.w16[ps.count++] = h->peers.w16[q] + h->shard_begin;
@@ -297,9 +301,12 @@ int peer_step(slm_opt_handle* h, const void* dev, int dtype, const slm_step_conf
                                         h->grid_update[0], s, &ps),
                     "update kernel")))
     return st;
-  return h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotWeights, epoch,
-                                     h->d_state, tmo, s),
-                 "weights barrier");
+  if ((st = phase_mark(h, s))) return st;
+  if ((st = h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotWeights, epoch,
+                                        h->d_state, tmo, s),
+                    "weights barrier")))
+    return st;
+  return phase_mark(h, s);
 }
 
 }  // namespace
@@ -353,6 +360,7 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
     h->recv_bytes = need;
   }
   const ncclDataType_t type = elem_type(esize);
+  if ((st = phase_begin(h, s))) return st;
   // 1. slice q of this rank's gradient goes to rank q; slice r of every rank arrives here.
   ncclGroupStart();
   for (int q = 0; q < N; ++q) {
@@ -365,6 +373,7 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                comm_of(h), s);
   }
   if ((st = settle(h, ncclGroupEnd(), "gradient all-to-all"))) return st;
+  if ((st = phase_mark(h, s))) return st;
   // 2. rank-ordered sum + unscale + partials.
   const FinalizeParams fp = finalize_params(h, cfg);
   if ((st = h->cuda(launch_zero1_reduce(dtype, h->d_recv, uint32_t(N), S, h->shard_len,
@@ -372,15 +381,18 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                                         h->d_send, h->d_state, h->grid_norm, s),
                     "zero1 reduce kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   // 3. partials of every rank, 4. identical finalize everywhere.
   if ((st = settle(h, ncclAllGather(h->d_send, h->d_gathered, h->chunks_per_rank + 1,
                                     ncclFloat64, comm_of(h), s),
                    "partials all-gather")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   if ((st = h->cuda(launch_zero1_finalize(h->d_gathered, uint32_t(N), h->chunks_per_rank,
                                           h->d_scaler, h->d_state, fp, s),
                     "zero1 finalize kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   // 5. AdamW on the shard over the raw f32 sums (unscaled inside, as on one GPU).
   const AdamwParams p = adamw_params(cfg);
   if ((st = h->cuda(launch_adamw_update(SLM_DTYPE_F32, h->d_gsum, h->shard_len, h->shard_begin,
@@ -389,10 +401,13 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                                         h->grid_update[0], s),
                     "update kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   // 6. bf16 weights of every shard on every rank.
-  return settle(h, ncclAllGather(h->w16 + uint64_t(h->rank) * S, h->w16, S, ncclBfloat16,
-                                 comm_of(h), s),
-                "bf16 all-gather");
+  if ((st = settle(h, ncclAllGather(h->w16 + uint64_t(h->rank) * S, h->w16, S, ncclBfloat16,
+                                    comm_of(h), s),
+                   "bf16 all-gather")))
+    return st;
+  return phase_mark(h, s);
 }
 
 }  // namespace slmopt

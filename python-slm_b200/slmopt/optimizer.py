@@ -251,6 +251,21 @@ class B200Adamw:
         self._check(self.lib.slm_opt_read_result(self._h, ctypes.byref(res)))
         return res
 
+    def phase_timing(self, enable: bool = True) -> None:
+        """Record per-phase device times of each step (clears earlier sums).
+        Each step then waits for the previous one: keep it off in timed runs."""
+        self._check(self.lib.slm_opt_phase_timing(self._h, 1 if enable else 0))
+
+    def phase_times(self) -> tuple[dict[str, float], int]:
+        """Mean ms per phase of the steps timed since phase_timing(True), and
+        how many steps that was."""
+        out = (ctypes.c_double * 8)()
+        n, steps = ctypes.c_uint32(), ctypes.c_uint64()
+        self._check(self.lib.slm_opt_phase_times(self._h, out, 8, ctypes.byref(n),
+                                                 ctypes.byref(steps)))
+        names = [self.lib.slm_opt_phase_name(self._h, i).decode() for i in range(n.value)]
+        return {name: out[i] for i, name in enumerate(names)}, int(steps.value)
+
     def apply_normalized_clipped_gradients(self, gradients: np.ndarray, learning_rate: float,
                                            one_based_update: int, valid_targets: int = 0,
                                            with_sha: bool = True) -> str | None:

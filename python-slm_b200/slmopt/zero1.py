@@ -217,6 +217,18 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     if res.status != 0 or res.skipped:
         raise RuntimeError(f"timed step failed on rank {rank}: {res.as_dict()}")
 
+    # Phase split, outside the timed region (with timing on, each step first
+    # waits for the previous one); per phase the max over ranks.
+    opt.phase_timing(True)
+    for _ in range(min(50, max(K, 3))):
+        opt.step(dev, opts, stream=stream, wait=False)
+    opt.read_result()
+    times, _ = opt.phase_times()
+    opt.phase_timing(False)
+    tp = torch.tensor(list(times.values()), dtype=torch.float64)
+    dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+    phases_ms = {name: float(v) for name, v in zip(times, tp.tolist())}
+
     # End to end: the gradient from pinned host memory each step, result read back.
     host = torch.from_numpy(grads).pin_memory()
     E = max(3, args.e2e_steps)
@@ -256,6 +268,7 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
                     "ms_per_step": e2e_ms},
             "gpu_launches": (5 if opt_exchange == _lib.ZERO1_PEER else 3) * K,
             "exchange": "peer-memory" if opt_exchange == _lib.ZERO1_PEER else "nccl",
+            "phases_ms": phases_ms,
             "clocks": clk,
             "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale},
         }

@@ -221,6 +221,30 @@ def test_async_step_on_a_stream_then_read_result(torch):
     check_equal(res, got, ores, ost)
 
 
+def test_phase_timing_leaves_results_unchanged(torch):
+    table = TensorTable.from_sizes([200_003, 768])
+    n = table.parameter_count
+    grads = synth.grads_bf16(n, 8)
+    state = synth.optimizer_state(n, 8)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        opt.phase_timing(True)
+        dev = to_device(torch, grads)
+        for t in range(1, 5):
+            res = opt.step(dev, StepOptions(one_based_update=t, static_loss_scale=65536.0))
+        times, steps = opt.phase_times()
+        got = opt.read_state()
+        opt.phase_timing(False)
+        assert opt.phase_times() == ({}, 0)
+    assert steps == 4 and list(times) == ["norm pass", "update"]
+    assert all(ms > 0.0 for ms in times.values())
+    ost = {k: v.copy() for k, v in state.items()}
+    for t in range(1, 5):
+        ores = oracle.step(oracle.make_config(t=t, static_scale=65536.0), grads, table.offsets,
+                           table.decay, ost)
+    check_equal(res, got, ores, ost)
+
+
 def test_misaligned_device_gradients_are_rejected(torch):
     table = TensorTable.from_sizes([64])
     buf = torch.zeros(65, dtype=torch.float32, device="cuda")

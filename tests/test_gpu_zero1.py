@@ -63,6 +63,7 @@ def _rank_main(rank, world, port, table_name, exchange, out_q):
         grads = synth.grads_bf16(P, seed=rank)
         opts = StepOptions(learning_rate=3e-4, one_based_update=10,
                            loss_scale_mode=_lib.SCALE_DYNAMIC)
+        opt.phase_timing(True)  # events at the phase boundaries must not change a bit
         r1 = opt.step(torch.from_numpy(grads).cuda(), opts)
         state1 = opt.read_state()  # collective gather
         sha1 = opt.state_sha256()  # collective
@@ -82,11 +83,13 @@ def _rank_main(rank, world, port, table_name, exchange, out_q):
         r3 = opt.step(bad, StepOptions(
             learning_rate=3e-4, one_based_update=12, loss_scale_mode=_lib.SCALE_DYNAMIC))
         state3 = opt.read_state()
+        phases = opt.phase_times()
         scale = opt.loss_scale()
         opt.close()
         out_q.put((rank, {"exchange": got_exchange, "r1": r1.as_dict(), "r2": r2.as_dict(),
                           "r3": r3.as_dict(), "d3": _digest(state3), "d1": _digest(state1),
                           "d2": _digest(state2), "sha1": sha1, "scale": scale,
+                          "phases": phases,
                           "bf16": hashlib.sha256(state1["bf16"].tobytes()).hexdigest()}))
         dist.destroy_process_group()
     except Exception:
@@ -163,6 +166,10 @@ def test_zero1_equals_single_replica(table_name, exchange):
         assert p["d2"] == p["d1"]
         assert p["r3"]["skipped"] == 1 and p["r3"]["next_loss_scale"] == 16384.0
         assert p["scale"][0] == 16384.0 and p["d3"] == p["d1"]
+        times, steps = p["phases"]
+        assert steps == 3
+        assert len(times) == (5 if exchange == "peer" else 6)
+        assert all(ms >= 0.0 for ms in times.values()) and sum(times.values()) > 0.0
 
 
 STRESS_STEPS = 100

@@ -182,6 +182,16 @@ int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
 /* Wait for the handle's last enqueued step on its stream and return its result. */
 int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out);
 
+/* The bf16 weights as f32 -- each value exactly bf16_bits_to_f32 of the bf16
+ * copy, the values the reference reloads into its graph after every update
+ * (CudaTrainerBackend::reload_graph, src/train/cuda_backend.rs:169-177 ->
+ * FullModelGraph::load, src/model/accelerator/full_model.rs:212-251) -- written
+ * on the device into dst_device (n == P floats, 16-byte aligned, PARAM-001
+ * order; a [rows, columns] tensor is its row-major slice), enqueued on
+ * `stream` after the step.  No host round trip; a ZeRO-1 handle exports its
+ * full gathered copy. */
+int slm_opt_export_weights_f32(slm_opt_handle* h, float* dst_device, uint64_t n, void* stream);
+
 /* Per-phase device timing of slm_opt_step (diagnostics; no counterpart in the
  * reference, whose step is one host loop).  While enabled, every step records
  * CUDA events on its stream at its phase boundaries, and the next step first

@@ -169,6 +169,7 @@ int allocate_state(slm_opt_handle* h, uint64_t w16_elems) {
   SLM_TRY(cudaMemcpy(h->d_scaler, &sc, sizeof(sc), cudaMemcpyHostToDevice), "upload scaler");
 #undef SLM_TRY
   h->grid_norm = norm_partials_grid(h->device);
+  h->grid_norm_bulk = norm_bulk_grid(h->device);
   h->grid_update[0] = adamw_update_grid(h->device, 0);
   h->grid_update[1] = adamw_update_grid(h->device, 1);
   return SLM_OK;
@@ -256,7 +257,7 @@ int enqueue_norm(slm_opt_handle* h, const void* dev_grads, int dtype, const slm_
                  cudaStream_t s) {
   const FinalizeParams fp = finalize_params(h, cfg);
   return h->cuda(launch_norm_partials(dtype, dev_grads, h->P, 0, h->n_chunks, h->d_scaler,
-                                      h->d_partials, h->d_state, fp, h->grid_norm, s),
+                                      h->d_partials, h->d_state, fp, h->grid_norm_bulk, s),
                  "norm kernel");
 }
 
@@ -698,6 +699,17 @@ int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out) {
   if (st) return st;
   h->pending = false;
   return finish_result(h, ds, out);
+}
+
+int slm_opt_export_weights_f32(slm_opt_handle* h, float* dst_device, uint64_t n, void* stream) {
+  if (!h || !dst_device) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (n != h->P)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "the f32 weight buffer must hold every parameter");
+  if (reinterpret_cast<uintptr_t>(dst_device) % 16 != 0)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "the f32 weight buffer must be 16-byte aligned");
+  DeviceGuard guard(h->device);
+  return h->cuda(launch_export_f32(h->w16, dst_device, h->P, static_cast<cudaStream_t>(stream)),
+                 "weight export kernel");
 }
 
 int slm_opt_phase_timing(slm_opt_handle* h, int enable) {

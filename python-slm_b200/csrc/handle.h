@@ -91,7 +91,8 @@ struct slm_opt_handle {
   size_t staging_bytes = 0;
   slmopt::DeviceStepState* h_state = nullptr;  // pinned
 
-  int grid_norm = 0;
+  int grid_norm = 0;       // resident blocks of the per-chunk tree kernels
+  int grid_norm_bulk = 0;  // persistent grid of the bulk-copy norm pass
   int grid_update[2] = {0, 0};
   // Gradients seen by the last norm pass (consumed by the update pass).
   const void* pass_grads = nullptr;

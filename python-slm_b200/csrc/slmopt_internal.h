@@ -53,6 +53,17 @@ constexpr uint32_t kBulkStages = SLM_BULK_STAGES;
 constexpr bool kUpdateBulk = SLM_UPDATE_BULK != 0;
 // Norm pass: vector loads issued together before their squares are added.
 constexpr uint32_t kNormBatch = 8;
+// Bulk-copy norm pass (SLM_NORM_BULK=1): a persistent grid streams each whole
+// chunk through kNormStages shared-memory stages of kNormStageBytes.
+#ifndef SLM_NORM_BULK
+#define SLM_NORM_BULK 1
+#endif
+#ifndef SLM_NORM_STAGES
+#define SLM_NORM_STAGES 6
+#endif
+constexpr bool kNormBulk = SLM_NORM_BULK != 0;
+constexpr uint32_t kNormStages = SLM_NORM_STAGES;
+constexpr uint32_t kNormStageBytes = 16384;
 
 struct DeviceScaler {
   float scale;
@@ -174,12 +185,17 @@ cudaError_t launch_accumulate_norm(int dtype, float* acc, const void* micro, uin
                                    int overwrite, uint32_t n_chunks, DeviceScaler* scaler,
                                    double* partials, DeviceStepState* st,
                                    const FinalizeParams& fp, cudaStream_t stream);
+// f32 copy of the bf16 weights (n elements, both 16-byte aligned).
+cudaError_t launch_export_f32(const uint16_t* w16, float* dst, uint64_t n, cudaStream_t stream);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,
                                   const float* variance, const uint16_t* w16, uint64_t n,
                                   uint32_t* bad_flag, cudaStream_t stream);
 int norm_partials_grid(int device);
+// Persistent grid of the bulk-copy norm pass (sets its shared-memory limit on
+// the current device).
+int norm_bulk_grid(int device);
 int adamw_update_grid(int device, int dtype);
 
 }  // namespace slmopt

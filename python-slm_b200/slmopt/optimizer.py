@@ -171,6 +171,21 @@ class B200Adamw:
     def validate(self) -> None:
         self._check(self.lib.slm_opt_validate_state(self._h))
 
+    def export_weights_f32(self, out=None, stream=None):
+        """The bf16 weights as an f32 CUDA tensor of P elements (the values the
+        reference's graph reload uploads), written on the device on `stream`."""
+        import torch
+
+        P = self.P
+        if out is None:
+            out = torch.empty(P, dtype=torch.float32, device=f"cuda:{self.device}")
+        if out.dtype != torch.float32 or not out.is_cuda or not out.is_contiguous() or \
+                out.numel() != P:
+            raise ValueError("out must be a contiguous f32 CUDA tensor of P elements")
+        self._check(self.lib.slm_opt_export_weights_f32(self._h, out.data_ptr(), P,
+                                                        _stream_handle(stream)))
+        return out
+
     def state_sha256(self) -> str:
         buf = ctypes.create_string_buffer(65)
         self._check(self.lib.slm_opt_state_sha256(self._h, buf))

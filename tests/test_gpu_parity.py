@@ -245,6 +245,25 @@ def test_phase_timing_leaves_results_unchanged(torch):
     check_equal(res, got, ores, ost)
 
 
+def test_export_weights_f32_is_the_graph_reload_values(torch):
+    # after a step, the f32 export equals bf16_bits_to_f32 of the bf16 copy,
+    # which the oracle's step produced bit-exactly
+    table = TensorTable.from_sizes([65536 * 2 + 24, 768, 13])
+    n = table.parameter_count
+    grads = synth.grads_bf16(n, 9)
+    state = synth.optimizer_state(n, 9)
+    opts = StepOptions(one_based_update=5, static_loss_scale=65536.0)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        opt.step(to_device(torch, grads), opts)
+        w = opt.export_weights_f32().cpu().numpy()
+        with pytest.raises(ValueError):
+            opt.export_weights_f32(torch.empty(n - 1, dtype=torch.float32, device="cuda"))
+    ost = {k: v.copy() for k, v in state.items()}
+    oracle.step(oracle_config(opts), grads, table.offsets, table.decay, ost)
+    assert_same_bits(w, synth.bf16_bits_to_f32(ost["bf16"]), "f32 weights")
+
+
 def test_misaligned_device_gradients_are_rejected(torch):
     table = TensorTable.from_sizes([64])
     buf = torch.zeros(65, dtype=torch.float32, device="cuda")

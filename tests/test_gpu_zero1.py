@@ -67,6 +67,9 @@ def _rank_main(rank, world, port, table_name, exchange, out_q):
         r1 = opt.step(torch.from_numpy(grads).cuda(), opts)
         state1 = opt.read_state()  # collective gather
         sha1 = opt.state_sha256()  # collective
+        w32 = opt.export_weights_f32().cpu().numpy()  # this rank's full copy
+        w32_ok = bool(np.array_equal(w32.view(np.uint32),
+                                     synth.bf16_bits_to_f32(state1["bf16"]).view(np.uint32)))
         bad = grads.copy()
         if rank == world - 1:
             synth.inject_nonfinite(bad, 5, table.offsets)
@@ -89,7 +92,7 @@ def _rank_main(rank, world, port, table_name, exchange, out_q):
         out_q.put((rank, {"exchange": got_exchange, "r1": r1.as_dict(), "r2": r2.as_dict(),
                           "r3": r3.as_dict(), "d3": _digest(state3), "d1": _digest(state1),
                           "d2": _digest(state2), "sha1": sha1, "scale": scale,
-                          "phases": phases,
+                          "phases": phases, "w32_ok": w32_ok,
                           "bf16": hashlib.sha256(state1["bf16"].tobytes()).hexdigest()}))
         dist.destroy_process_group()
     except Exception:
@@ -166,6 +169,7 @@ def test_zero1_equals_single_replica(table_name, exchange):
         assert p["d2"] == p["d1"]
         assert p["r3"]["skipped"] == 1 and p["r3"]["next_loss_scale"] == 16384.0
         assert p["scale"][0] == 16384.0 and p["d3"] == p["d1"]
+        assert p["w32_ok"]
         times, steps = p["phases"]
         assert steps == 3
         assert len(times) == (5 if exchange == "peer" else 6)

@@ -44,10 +44,10 @@ FALLBACK_HBM_GBS = 6650.0
 # read g (2 or 4) + master/m/v (12), write master/m/v (12) + bf16 (2).
 UPDATE_BYTES = {"mixed": 28, "fp32": 30}
 STEP_BYTES = {"mixed": 30, "fp32": 34}  # + the norm pass's read of g
-# dram__bytes_read.sum + dram__bytes_write.sum of one update-kernel launch,
-# from one ncu capture of a 33,554,432-parameter prefix scaled by parameter
-# count to the full launch; None where no capture exists.
-UPDATE_TRAFFIC_BYTES = {"mixed": 3.555e9, "fp32": None}
+# dram__bytes_read.sum + dram__bytes_write.sum of one full-size update-kernel
+# launch (135,285,504 params, one-pass ncu capture, cold cache); None where no
+# capture exists.
+UPDATE_TRAFFIC_BYTES = {"mixed": 3.725e9, "fp32": None}
 
 
 def parse_args():

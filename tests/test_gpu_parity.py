@@ -264,6 +264,31 @@ def test_export_weights_f32_is_the_graph_reload_values(torch):
     assert_same_bits(w, synth.bf16_bits_to_f32(ost["bf16"]), "f32 weights")
 
 
+@pytest.mark.parametrize("t", [1, 3, 10, 200, 1000])
+def test_wide_exponent_moments_bit_exact(torch, t):
+    # m and v spread over (almost) every f32 exponent, with zeros, -0.0 and
+    # subnormals (kept: the library builds with -ftz=false): the divisions,
+    # the square root and the bf16 rounding must equal the oracle's bit for
+    # bit at the edges of the range too, for small and large t.
+    table = TensorTable.from_sizes([70_000, 4101], [True, False])
+    n = table.parameter_count
+    rng = np.random.default_rng(t)
+    state = synth.optimizer_state(n, 12)
+    sign = np.where(rng.random(n) < 0.5, -1.0, 1.0)
+    m = (sign * np.exp2(rng.uniform(-149, 20, n))).astype(np.float32)
+    v = np.exp2(rng.uniform(-149, 40, n)).astype(np.float32)
+    m[:64] = 0.0
+    m[64:128] = -0.0
+    v[:32] = 0.0
+    m[128:192] = (np.arange(64) * np.float32(2.0**-149)).astype(np.float32)  # subnormals
+    state["moment"], state["variance"] = m, v
+    grads = synth.grads_f32(n, 12)
+    grads[200:264] = 0.0
+    opts = StepOptions(one_based_update=t)
+    res, got, ores, ost = run_both(torch, table, grads, opts, state=state)
+    check_equal(res, got, ores, ost)
+
+
 def test_misaligned_device_gradients_are_rejected(torch):
     table = TensorTable.from_sizes([64])
     buf = torch.zeros(65, dtype=torch.float32, device="cuda")

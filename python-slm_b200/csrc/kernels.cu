@@ -1197,14 +1197,17 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
 // Flag barrier between the ranks of one node: lane q announces this rank's
 // arrival (the step's epoch) in rank q's flag array, then waits until rank q
 // has announced itself here.  Epochs only grow, so flags are never reset; the
-// wait is bounded and records kernel_error instead of hanging.
+// wait is bounded and records kernel_error instead of hanging.  Once a wait of
+// this step has given up, later barriers of the step only announce: the step
+// has failed here, and a peer still inside it fails at its own bounded wait.
 __global__ void peer_barrier_kernel(PeerTable pt, int rank, int world, uint32_t slot,
                                     uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns) {
   const int q = threadIdx.x;
+  const bool failed = st->kernel_error != 0u;  // written by earlier kernels of this stream
   __threadfence_system();
   if (q < world)
     *reinterpret_cast<volatile uint32_t*>(pt.flags[q] + slot * kMaxRanks + rank) = epoch;
-  if (q < world) {
+  if (q < world && !failed) {
     const volatile uint32_t* mine = pt.flags[rank] + slot * kMaxRanks + q;
     const uint64_t t0 = global_ns();
     while (static_cast<int32_t>(*mine - epoch) < 0) {

@@ -86,8 +86,21 @@ ncclDataType_t elem_type(size_t bytes) {
 
 namespace slmopt {
 
+// Bound of each device-side wait of the peer exchange: the handle's timeout,
+// at most 10 s.
+uint64_t peer_wait_ms(const slm_opt_handle* h) {
+  return h->timeout_ms < 10000u ? h->timeout_ms : 10000u;
+}
+
 int zero1_wait(slm_opt_handle* h, cudaStream_t s) {
   const auto t0 = Clock::now();
+  // Over peer memory every device wait of a step is bounded (two barriers and
+  // the finalize, each by barrier_timeout_ns), so the host allows for all of
+  // them: a missing rank is then reported by the device and the stream has
+  // drained when this returns.
+  const uint64_t limit_ms =
+      h->exchange == SLM_ZERO1_PEER ? uint64_t(h->timeout_ms) + 3ull * peer_wait_ms(h)
+                                    : uint64_t(h->timeout_ms);
   for (;;) {
     const cudaError_t e = cudaStreamQuery(s);
     if (e == cudaSuccess) return SLM_OK;
@@ -98,7 +111,7 @@ int zero1_wait(slm_opt_handle* h, cudaStream_t s) {
       if (state != ncclSuccess && state != ncclInProgress)
         return nccl_fail(h, state, "collective failed");
     }
-    if (elapsed_ms(t0) > h->timeout_ms) {
+    if (elapsed_ms(t0) > limit_ms) {
       abort_comm(h);
       return h->err(SLM_ERR_TIMEOUT, "the step did not complete within the timeout; a rank "
                                      "stopped participating");
@@ -261,10 +274,7 @@ int setup_peer_exchange(slm_opt_handle* h, cudaStream_t s) {
 
 namespace {
 
-uint64_t barrier_timeout_ns(const slm_opt_handle* h) {
-  const uint64_t ms = h->timeout_ms < 10000u ? h->timeout_ms : 10000u;
-  return ms * 1000000ull;
-}
+uint64_t barrier_timeout_ns(const slm_opt_handle* h) { return peer_wait_ms(h) * 1000000ull; }
 
 // One ZeRO-1 step over peer memory, all on stream s (see slm_opt_zero1_set_exchange).
 int peer_step(slm_opt_handle* h, const void* dev, int dtype, const slm_step_config* cfg,

@@ -283,3 +283,103 @@ def test_zero1_stress_trajectory_matches_oracle():
     want = _digest(state)
     for r, p in res.items():
         assert p["runs"][0][1] == want, f"rank {r} final state differs from the oracle"
+
+
+def _absent_peer_rank(rank, world, port, out_q):
+    # Failure detection on the device, without faulting anything: after one
+    # good step rank 1 stops stepping (it stays alive, its memory mapped, none
+    # of its kernels in flight).  Rank 0's next step waits at the gradient
+    # barrier for a flag nothing sets; the bounded wait gives up after the
+    # handle's timeout and the step reports SLM_ERR_TIMEOUT.  Later, rank 1
+    # steps alone: it passes the barrier (rank 0 announced itself) and its
+    # finalize waits for partials rank 0 never sends, with the same outcome.
+    try:
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from slmopt import SlmError, StepOptions, _lib
+        from slmopt.zero1 import Zero1Adamw, unique_id
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=120))
+        table = _table("ragged")
+        P = table.parameter_count
+        ids = [unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        opt = Zero1Adamw(table, rank, world, ids[0], device=rank, timeout_ms=2000)
+        out = {"exchange": opt.exchange}
+        st = synth.optimizer_state(P, 0)
+        opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+        grads = torch.from_numpy(synth.grads_bf16(P, seed=rank)).cuda()
+        opts = StepOptions(learning_rate=3e-4, one_based_update=1, static_loss_scale=65536.0)
+        out["r1"] = opt.step(grads, opts).status
+
+        def failing_step(t):
+            t0 = time.time()
+            try:
+                opt.step(grads, StepOptions(learning_rate=3e-4, one_based_update=t,
+                                            static_loss_scale=65536.0))
+                return ("ok", time.time() - t0)
+            except SlmError as e:
+                return (e.status, time.time() - t0)
+
+        dist.barrier()
+        if rank == 0:
+            out["alone"] = failing_step(2)
+            out["after"] = failing_step(3)  # the handle is broken: fails at once
+            torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 1:
+            out["alone"] = failing_step(2)
+            torch.cuda.synchronize()
+        dist.barrier()  # nobody's kernels in flight before any memory is released
+        opt.close()
+        out_q.put((rank, out))
+        dist.destroy_process_group()
+    except Exception:
+        out_q.put((rank, {"error": traceback.format_exc()}))
+
+
+def test_absent_peer_times_out_on_device():
+    n = _gpus()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    from slmopt import _lib
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_absent_peer_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res, deadline = {}, time.time() + 300
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, payload = q.get(timeout=2.0)
+            res[r] = payload
+        except Exception:
+            if all(not p.is_alive() for p in procs) and q.empty():
+                break
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert len(res) == world, res
+    for r, p in res.items():
+        assert "error" not in p, p["error"]
+        assert p["exchange"] == _lib.ZERO1_PEER
+        assert p["r1"] == 0
+        status, seconds = p["alone"]
+        assert status == _lib.SLM_ERR_TIMEOUT, p
+        assert 1.5 < seconds < 10.0, p  # the 2 s device bound, not the host's
+    status, seconds = res[0]["after"]
+    assert status == _lib.SLM_ERR_TIMEOUT and seconds < 1.0, res[0]

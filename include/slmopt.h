@@ -182,6 +182,24 @@ int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
 /* Wait for the handle's last enqueued step on its stream and return its result. */
 int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out);
 
+/* Pipelined host gradients (the reference hands apply_update a host slice
+ * every update, src/train/trainer.rs:902-904).  slm_opt_step with host memory
+ * uploads on the step's own stream, so the PCIe copy and the step's kernels
+ * run one after the other.  slm_opt_upload_gradients instead copies P
+ * gradients of `dtype` from host memory (pinned for an asynchronous copy)
+ * into one of two device slots on the handle's own copy stream and returns
+ * the slot; slm_opt_step_uploaded(slot) then runs the step on `stream` once
+ * that copy has landed.  Uploading the next update's gradients before
+ * stepping on the current ones overlaps the copy with the step.  The copy
+ * does not wait for earlier work on any caller stream: the host buffer must
+ * hold its final contents when the upload is called and stay valid until the
+ * step that uses it has run.  A slot is rewritten only after the step that
+ * read it; a third upload before either slot was stepped on is rejected. */
+int slm_opt_upload_gradients(slm_opt_handle* h, const void* grads_host, int dtype,
+                             int* slot_out);
+int slm_opt_step_uploaded(slm_opt_handle* h, int slot, const slm_step_config* cfg,
+                          slm_step_result* out, void* stream);
+
 /* The bf16 weights as f32 -- each value exactly bf16_bits_to_f32 of the bf16
  * copy, the values the reference reloads into its graph after every update
  * (CudaTrainerBackend::reload_graph, src/train/cuda_backend.rs:169-177 ->

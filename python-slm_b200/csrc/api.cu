@@ -473,6 +473,16 @@ int slm_opt_destroy(slm_opt_handle* h) {
   cudaFree(h->d_scaler);
   cudaFree(h->d_flag);
   cudaFree(h->d_staging);
+  if (h->copy_stream) {
+    cudaStreamSynchronize(h->copy_stream);
+    cudaStreamDestroy(h->copy_stream);
+  }
+  for (auto& u : h->up) {
+    if (u.consumed_recorded) cudaEventSynchronize(u.consumed);
+    cudaFree(u.dev);
+    if (u.uploaded) cudaEventDestroy(u.uploaded);
+    if (u.consumed) cudaEventDestroy(u.consumed);
+  }
   if (h->h_state) cudaFreeHost(h->h_state);
   delete h;
   return SLM_OK;
@@ -659,17 +669,13 @@ int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* str
   return st;
 }
 
-int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
-                 const slm_step_config* cfg, slm_step_result* out, void* stream) {
-  if (!h || !grads) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
-  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
-    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
-  int st = check_config(h, cfg);
-  if (st) return st;
-  if (h->broken)
-    return h->err(SLM_ERR_TIMEOUT, "a previous collective timed out; the communicator is closed");
-  DeviceGuard guard(h->device);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+namespace {
+
+// Enqueues one whole step on s (both passes, or the ZeRO-1 step); waits for
+// and returns the result when out != NULL.
+int run_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
+             const slm_step_config* cfg, slm_step_result* out, cudaStream_t s) {
+  int st = SLM_OK;
   if (h->sharded()) {
     if ((st = zero1_step(h, grads, dtype, memory, cfg, s))) return st;
   } else {
@@ -684,6 +690,103 @@ int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
   phase_end(h);
   h->pending = true;
   h->pending_stream = s;
+  if (!out) return SLM_OK;
+  DeviceStepState ds;
+  if ((st = read_state(h, s, &ds))) return st;
+  h->pending = false;
+  return finish_result(h, ds, out);
+}
+
+int release_slot(slm_opt_handle* h, slm_opt_handle::UploadSlot* slot, cudaStream_t s) {
+  slot->filled = false;
+  slot->consumed_recorded = true;
+  return h->cuda(cudaEventRecord(slot->consumed, s), "upload slot release");
+}
+
+}  // namespace
+
+int slm_opt_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
+                 const slm_step_config* cfg, slm_step_result* out, void* stream) {
+  if (!h || !grads) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  int st = check_config(h, cfg);
+  if (st) return st;
+  if (h->broken)
+    return h->err(SLM_ERR_TIMEOUT, "a previous collective timed out; the communicator is closed");
+  DeviceGuard guard(h->device);
+  return run_step(h, grads, dtype, memory, cfg, out, static_cast<cudaStream_t>(stream));
+}
+
+int slm_opt_upload_gradients(slm_opt_handle* h, const void* grads_host, int dtype,
+                             int* slot_out) {
+  if (!h || !grads_host || !slot_out) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  DeviceGuard guard(h->device);
+  int st;
+  if (!h->copy_stream &&
+      (st = h->cuda(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking),
+                    "copy stream")))
+    return st;
+  const int k = h->next_up;
+  slm_opt_handle::UploadSlot& u = h->up[k];
+  if (u.filled)
+    return h->err(SLM_ERR_INVALID_ARGUMENT,
+                  "both upload slots hold gradients that no step has used yet");
+  if (!u.uploaded) {
+    if ((st = h->cuda(cudaEventCreateWithFlags(&u.uploaded, cudaEventDisableTiming), "event")) ||
+        (st = h->cuda(cudaEventCreateWithFlags(&u.consumed, cudaEventDisableTiming), "event")))
+      return st;
+  }
+  const size_t bytes = h->P * (dtype == SLM_DTYPE_F32 ? 4 : 2);
+  if (u.bytes < bytes) {
+    if (u.consumed_recorded &&
+        (st = h->cuda(cudaEventSynchronize(u.consumed), "upload slot wait")))
+      return st;
+    cudaFree(u.dev);
+    u.dev = nullptr;
+    u.bytes = 0;
+    if ((st = h->cuda(cudaMalloc(&u.dev, bytes), "cudaMalloc upload slot"))) return st;
+    u.bytes = bytes;
+  }
+  // The slot is rewritten only after the last step that read it.
+  if (u.consumed_recorded &&
+      (st = h->cuda(cudaStreamWaitEvent(h->copy_stream, u.consumed, 0), "upload slot wait")))
+    return st;
+  if ((st = h->cuda(cudaMemcpyAsync(u.dev, grads_host, bytes, cudaMemcpyHostToDevice,
+                                    h->copy_stream),
+                    "gradient upload")) ||
+      (st = h->cuda(cudaEventRecord(u.uploaded, h->copy_stream), "gradient upload")))
+    return st;
+  u.filled = true;
+  u.dtype = dtype;
+  h->next_up ^= 1;
+  *slot_out = k;
+  return SLM_OK;
+}
+
+int slm_opt_step_uploaded(slm_opt_handle* h, int slot, const slm_step_config* cfg,
+                          slm_step_result* out, void* stream) {
+  if (!h) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL handle");
+  if (slot != 0 && slot != 1) return h->err(SLM_ERR_INVALID_ARGUMENT, "upload slot must be 0 or 1");
+  slm_opt_handle::UploadSlot& u = h->up[slot];
+  if (!u.filled)
+    return h->err(SLM_ERR_INVALID_ARGUMENT, "the upload slot holds no gradients to step on");
+  int st = check_config(h, cfg);
+  if (st) return st;
+  if (h->broken)
+    return h->err(SLM_ERR_TIMEOUT, "a previous collective timed out; the communicator is closed");
+  DeviceGuard guard(h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = h->cuda(cudaStreamWaitEvent(s, u.uploaded, 0), "upload wait"))) return st;
+  // Enqueue, then mark the slot read (even if the enqueue failed part-way, so
+  // that the next upload into it waits for whatever did get enqueued), then
+  // collect the result.
+  st = run_step(h, u.dev, u.dtype, SLM_MEMORY_DEVICE, cfg, nullptr, s);
+  const int rel = release_slot(h, &u, s);
+  if (st) return st;
+  if (rel) return rel;
   if (!out) return SLM_OK;
   DeviceStepState ds;
   if ((st = read_state(h, s, &ds))) return st;

@@ -101,6 +101,20 @@ struct slm_opt_handle {
   bool pending = false;
   std::string last_error = "no error";
 
+  // Pipelined gradient uploads (slm_opt_upload_gradients / slm_opt_step_uploaded):
+  // two device slots filled from host memory on the handle's own copy stream.
+  struct UploadSlot {
+    void* dev = nullptr;
+    size_t bytes = 0;
+    int dtype = -1;
+    bool filled = false;             // uploaded, not yet handed to a step
+    bool consumed_recorded = false;  // `consumed` marks the last step that read it
+    cudaEvent_t uploaded = nullptr;
+    cudaEvent_t consumed = nullptr;
+  } up[2];
+  cudaStream_t copy_stream = nullptr;
+  int next_up = 0;
+
   // ---- ZeRO-1 (world > 1) ---------------------------------------------------
   int rank = 0, world = 1;
   void* comm = nullptr;            // ncclComm_t

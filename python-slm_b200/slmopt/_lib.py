@@ -139,6 +139,9 @@ SIGNATURES = [
     ("slm_opt_state_sha256", _I, [_P, ctypes.c_char_p]),
     ("slm_opt_step", _I, [_P, _P, _I, _I, ctypes.POINTER(StepConfig), ctypes.POINTER(StepResult), _P]),
     ("slm_opt_read_result", _I, [_P, ctypes.POINTER(StepResult)]),
+    ("slm_opt_upload_gradients", _I, [_P, _P, _I, ctypes.POINTER(_I)]),
+    ("slm_opt_step_uploaded", _I, [_P, _I, ctypes.POINTER(StepConfig),
+                                   ctypes.POINTER(StepResult), _P]),
     ("slm_opt_export_weights_f32", _I, [_P, _P, _U64, _P]),
     ("slm_opt_phase_timing", _I, [_P, _I]),
     ("slm_opt_phase_times", _I, [_P, ctypes.POINTER(ctypes.c_double), _U32,

@@ -222,6 +222,36 @@ class B200Adamw:
         self._check(self.lib.slm_opt_step(self._h, ptr, dt, mem, ctypes.byref(cfg), None, s))
         return None
 
+    def upload(self, grads) -> int:
+        """Start copying host gradients (numpy array or CPU tensor, pinned for
+        an asynchronous copy) into a device slot on the handle's copy stream;
+        returns the slot for step_uploaded.  The buffer is kept alive here
+        until the slot is reused."""
+        ptr, dt, mem, n, keep = _grad_pointer(grads)
+        if mem != _lib.MEMORY_HOST:
+            raise ValueError("upload takes host gradients")
+        if n != self.P:
+            raise ValueError(f"expected {self.P} gradients, got {n}")
+        slot = ctypes.c_int()
+        self._check(self.lib.slm_opt_upload_gradients(self._h, ptr, dt, ctypes.byref(slot)))
+        if not hasattr(self, "_upload_keep"):
+            self._upload_keep = [None, None]
+        self._upload_keep[slot.value] = keep
+        return slot.value
+
+    def step_uploaded(self, slot: int, options: StepOptions | None = None, stream=None,
+                      wait: bool = True) -> _lib.StepResult | None:
+        """The fused step over the gradients of an upload slot (see step)."""
+        cfg = (options or StepOptions()).to_c()
+        s = _stream_handle(stream)
+        if wait:
+            res = _lib.StepResult()
+            self._check(self.lib.slm_opt_step_uploaded(self._h, slot, ctypes.byref(cfg),
+                                                       ctypes.byref(res), s))
+            return res
+        self._check(self.lib.slm_opt_step_uploaded(self._h, slot, ctypes.byref(cfg), None, s))
+        return None
+
     def norm_pass(self, grads, options: StepOptions | None = None, stream=None):
         """Enqueue the unscale / non-finite / norm / clip pass; returns the
         keep-alive object that must outlive the matching update_pass."""

@@ -289,6 +289,45 @@ def test_wide_exponent_moments_bit_exact(torch, t):
     check_equal(res, got, ores, ost)
 
 
+def test_pipelined_uploads_match_oracle(torch):
+    # the next update's gradients are uploaded before stepping on the current
+    # ones (copy on the handle's stream, step on the caller's): same results
+    # as the oracle's sequential steps; misuse is rejected
+    table = TensorTable.from_sizes([65536 * 3 + 5, 768], [True, False])
+    n = table.parameter_count
+    steps = 5
+    grads = [synth.grads_bf16(n, 100 + t) for t in range(steps)]
+    pinned = [torch.from_numpy(g.view(np.int16)).pin_memory() for g in grads]
+    state = synth.optimizer_state(n, 14)
+    s = torch.cuda.Stream()
+    res = []
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        opt.set_loss_scale(65536.0)
+        slot = opt.upload(pinned[0])
+        for t in range(1, steps + 1):
+            nxt = opt.upload(pinned[t]) if t < steps else None
+            if t == 1:
+                with pytest.raises(SlmError) as e:
+                    opt.upload(pinned[0])  # both slots hold gradients not yet stepped on
+                assert e.value.status == _lib.SLM_ERR_INVALID_ARGUMENT
+            res.append(opt.step_uploaded(slot, StepOptions(
+                one_based_update=t, loss_scale_mode=_lib.SCALE_DYNAMIC), stream=s))
+            slot = nxt
+        with pytest.raises(SlmError):
+            opt.step_uploaded(0, StepOptions(one_based_update=9))  # nothing uploaded there
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in state.items()}
+    scaler = oracle.Scaler(65536.0, 0)
+    for t in range(1, steps + 1):
+        ores = oracle.step(oracle.make_config(t=t, dynamic=True), grads[t - 1], table.offsets,
+                           table.decay, ost, scaler)
+        assert res[t - 1].sum_squares == ores.sum_squares, t
+        assert np.float32(res[t - 1].clip_scale) == np.float32(ores.clip_scale), t
+    for key in ("master", "moment", "variance", "bf16"):
+        assert_same_bits(got[key], ost[key], key)
+
+
 def test_misaligned_device_gradients_are_rejected(torch):
     table = TensorTable.from_sizes([64])
     buf = torch.zeros(65, dtype=torch.float32, device="cuda")

@@ -139,6 +139,7 @@ void slm_step_config_default(slm_step_config* cfg);
  * Rejects empty tables, empty or duplicate names. */
 int slm_opt_create(const slm_tensor_spec* table, uint32_t n_tensors, int device,
                    slm_opt_handle** out);
+/* Waits for the device's outstanding work, then frees the handle. */
 int slm_opt_destroy(slm_opt_handle* h);
 uint64_t slm_opt_parameter_count(const slm_opt_handle* h);
 /* Human-readable detail of the handle's last failure (never NULL). */
@@ -290,7 +291,14 @@ int slm_opt_norm_pass_accumulate(slm_opt_handle* h, float* acc_device, const voi
  * the same order): slm_opt_create_zero1, slm_opt_step, slm_opt_init_master,
  * slm_opt_snapshot of a full f32 role, slm_opt_state_sha256.  Waits are
  * bounded by timeout_ms (0 = 300 s); on expiry the communicator is aborted and
- * the call returns SLM_ERR_TIMEOUT. */
+ * the call returns SLM_ERR_TIMEOUT.  With the peer-memory exchange (the
+ * default when every rank can map every other rank's memory) each device-side
+ * wait is bounded by min(timeout_ms, 10 s); a rank that gives up reports
+ * SLM_ERR_TIMEOUT from the step and its handle refuses further steps.
+ * Teardown: the ranks read and write each other's buffers during a step, so
+ * after a failed step every rank should return from its own step (each is
+ * bounded) and the ranks should agree on the host before any of them calls
+ * slm_opt_destroy, which frees the buffers the others have mapped. */
 
 /* A fresh NCCL unique id (128 bytes) for rank 0 to share with the others. */
 int slm_zero1_unique_id(uint8_t out[128]);

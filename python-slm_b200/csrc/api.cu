@@ -458,6 +458,9 @@ int slm_opt_create(const slm_tensor_spec* table, uint32_t n_tensors, int device,
 int slm_opt_destroy(slm_opt_handle* h) {
   if (!h) return SLM_OK;
   DeviceGuard guard(h->device);
+  // Work this handle enqueued (on any stream) finishes before its buffers and
+  // peer mappings go away; every kernel's waits are bounded.
+  cudaDeviceSynchronize();
   zero1_release(h);
   if (h->timer.created)
     for (cudaEvent_t e : h->timer.ev) cudaEventDestroy(e);

@@ -101,3 +101,46 @@ def test_create_rejects_bad_tables_before_touching_a_device():
     lib = _lib.load()
     h = ctypes.c_void_p()
     assert lib.slm_opt_create(None, 0, 0, ctypes.byref(h)) == _lib.SLM_ERR_P12_OPTIMIZER_STATE_INVALID
+
+
+def test_every_handle_entry_point_rejects_null_arguments():
+    # argument checks come before any device work, so these run without a GPU
+    lib = _lib.load()
+    cfg = _lib.StepConfig()
+    lib.slm_step_config_default(ctypes.byref(cfg))
+    res = _lib.StepResult()
+    i, u32, u64 = ctypes.c_int(), ctypes.c_uint32(), ctypes.c_uint64()
+    f, p, d = ctypes.c_float(), ctypes.c_void_p(), (ctypes.c_double * 8)()
+    buf = ctypes.create_string_buffer(128)
+    one = ctypes.c_float(1.0)
+    calls = {
+        "slm_opt_init_master": (None, None, None),
+        "slm_opt_snapshot": (None, 0, None, 0),
+        "slm_opt_restore": (None, 0, None, 0),
+        "slm_opt_validate_state": (None,),
+        "slm_opt_device_buffer": (None, 0, ctypes.byref(p)),
+        "slm_opt_state_sha256": (None, buf),
+        "slm_opt_step": (None, None, 1, 0, ctypes.byref(cfg), ctypes.byref(res), None),
+        "slm_opt_read_result": (None, ctypes.byref(res)),
+        "slm_opt_upload_gradients": (None, None, 1, ctypes.byref(i)),
+        "slm_opt_step_uploaded": (None, 0, ctypes.byref(cfg), None, None),
+        "slm_opt_norm_pass": (None, None, 1, 0, ctypes.byref(cfg), None),
+        "slm_opt_update_pass": (None, ctypes.byref(cfg), None),
+        "slm_opt_norm_pass_accumulate": (None, None, None, 1, 0, 0, ctypes.byref(cfg), None),
+        "slm_opt_apply_update": (None, None, 0, ctypes.c_float(3e-4), 1, 0, None),
+        "slm_opt_shard_range": (None, ctypes.byref(u64), ctypes.byref(u64)),
+        "slm_opt_zero1_set_exchange": (None, 0),
+        "slm_opt_gradient_buffer": (None, ctypes.byref(p), ctypes.byref(u64)),
+        "slm_opt_set_loss_scale": (None, one, 0),
+        "slm_opt_get_loss_scale": (None, ctypes.byref(f), ctypes.byref(u32)),
+        "slm_opt_export_weights_f32": (None, None, 0, None),
+        "slm_opt_phase_timing": (None, 1),
+        "slm_opt_phase_times": (None, d, 8, ctypes.byref(u32), ctypes.byref(u64)),
+        "slm_grad_accumulate": (None, None, 1, 0, 0, None),
+        "slm_grad_norm_noalloc": (None, 1, 10, one, one, None, None),
+    }
+    for name, args in calls.items():
+        assert getattr(lib, name)(*args) == _lib.SLM_ERR_INVALID_ARGUMENT, name
+        assert lib.slm_last_error_message().decode() != "no error", name
+    assert lib.slm_opt_destroy(None) == _lib.SLM_OK  # like free(NULL)
+    assert lib.slm_opt_phase_name(None, 0) is None

@@ -194,8 +194,10 @@ int slm_opt_read_result(slm_opt_handle* h, slm_step_result* out);
  * stepping on the current ones overlaps the copy with the step.  The copy
  * does not wait for earlier work on any caller stream: the host buffer must
  * hold its final contents when the upload is called and stay valid until the
- * step that uses it has run.  A slot is rewritten only after the step that
- * read it; a third upload before either slot was stepped on is rejected. */
+ * step that uses it has run.  Before reusing a slot the upload waits on the
+ * host until the step that read it has run (so the buffer of that slot's
+ * previous upload is free again when it returns); a third upload before
+ * either slot was stepped on is rejected. */
 int slm_opt_upload_gradients(slm_opt_handle* h, const void* grads_host, int dtype,
                              int* slot_out);
 int slm_opt_step_uploaded(slm_opt_handle* h, int slot, const slm_step_config* cfg,

@@ -742,21 +742,20 @@ int slm_opt_upload_gradients(slm_opt_handle* h, const void* grads_host, int dtyp
         (st = h->cuda(cudaEventCreateWithFlags(&u.consumed, cudaEventDisableTiming), "event")))
       return st;
   }
+  // The slot is rewritten only after the last step that read it has run; the
+  // host waits for that, so when this returns nothing on the device still
+  // refers to the host buffer of the slot's previous upload.
+  if (u.consumed_recorded &&
+      (st = h->cuda(cudaEventSynchronize(u.consumed), "upload slot wait")))
+    return st;
   const size_t bytes = h->P * (dtype == SLM_DTYPE_F32 ? 4 : 2);
   if (u.bytes < bytes) {
-    if (u.consumed_recorded &&
-        (st = h->cuda(cudaEventSynchronize(u.consumed), "upload slot wait")))
-      return st;
     cudaFree(u.dev);
     u.dev = nullptr;
     u.bytes = 0;
     if ((st = h->cuda(cudaMalloc(&u.dev, bytes), "cudaMalloc upload slot"))) return st;
     u.bytes = bytes;
   }
-  // The slot is rewritten only after the last step that read it.
-  if (u.consumed_recorded &&
-      (st = h->cuda(cudaStreamWaitEvent(h->copy_stream, u.consumed, 0), "upload slot wait")))
-    return st;
   if ((st = h->cuda(cudaMemcpyAsync(u.dev, grads_host, bytes, cudaMemcpyHostToDevice,
                                     h->copy_stream),
                     "gradient upload")) ||

@@ -226,7 +226,8 @@ class B200Adamw:
         """Start copying host gradients (numpy array or CPU tensor, pinned for
         an asynchronous copy) into a device slot on the handle's copy stream;
         returns the slot for step_uploaded.  The buffer is kept alive here
-        until the slot is reused."""
+        until the slot is reused (which first waits for the step that read
+        it), or the handle is closed."""
         ptr, dt, mem, n, keep = _grad_pointer(grads)
         if mem != _lib.MEMORY_HOST:
             raise ValueError("upload takes host gradients")

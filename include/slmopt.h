@@ -250,7 +250,11 @@ int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* str
  * CanonicalAdamw::apply_normalized_clipped_gradients, trainer.rs:222-295):
  * n must equal P (else P12_OPTIMIZER_GRADIENT_INVALID); non-finite gradients
  * fail with MODEL_GRADIENT_NONFINITE; the clip is re-verified (tolerance 0.05,
- * trainer.rs:161) over the fixed f64 tree; the lr must bit-equal
+ * trainer.rs:161) with the reference's own sequential f32 clip scale
+ * (gradient_clip_scale, src/model/oracle.rs:486-507, reproduced bit for bit
+ * on the device, so the accept / reject decision is the reference's even where
+ * that sum drifts from the exact one; ~0.3 s at 135M, an inherently serial
+ * sum); the lr must bit-equal
  * canonical_learning_rate(t) (P12_SCHEDULER_STATE_MISMATCH); AdamW runs with
  * OPT-001's constants and no further clip.  `grads_host` is host f32[n].
  * valid_targets is accepted and unused, as in the reference.  If out_sha256

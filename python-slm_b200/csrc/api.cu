@@ -890,8 +890,7 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   cfg.one_based_update = one_based_update >= 1 && one_based_update <= 0x7fffffffu
                              ? uint32_t(one_based_update)
                              : 1u;
-  cfg.apply_clip = 0;                  // the input is already clipped
-  cfg.min_clip_accept = 1.0f - 0.05f;  // CLIP_VERIFICATION_TOLERANCE, trainer.rs:161
+  cfg.apply_clip = 0;  // the input is already clipped
   cfg.nonfinite_policy = SLM_NONFINITE_ERROR;
   cfg.loss_scale_mode = SLM_SCALE_STATIC;
   cfg.static_loss_scale = 1.0f;
@@ -901,20 +900,28 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   const void* dev = nullptr;
   int st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev);
   if (st) return st;
-  // Re-verification first (trainer.rs:250-260): nothing is written on failure.
-  if ((st = enqueue_norm(h, dev, SLM_DTYPE_F32, &cfg, s))) return st;
+  // Re-verification first (trainer.rs:250-260), with the reference's own
+  // sequential f32 clip scale so that the accept / reject decision is the
+  // reference's; nothing is written on failure.
+  if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s),
+                    "clip check kernel")))
+    return st;
   DeviceStepState ds;
   if ((st = read_state(h, s, &ds))) return st;
-  if (ds.status != SLM_OK) {
-    if (ds.status == SLM_ERR_P12_OPTIMIZER_GRADIENT_INVALID) {
-      char msg[192];
-      std::snprintf(msg, sizeof(msg),
-                    "AdamW requires globally clipped FP32 gradients: update %llu re-measured a "
-                    "clip scale of %e, outside the 0.05 verification tolerance of 1.0",
-                    (unsigned long long)one_based_update, double(ds.clip_scale));
-      return h->err(ds.status, msg);
-    }
+  if (ds.kernel_error) return h->err(SLM_ERR_INTERNAL, "the clip check's copy pipeline stalled");
+  if (ds.status == SLM_ERR_MODEL_GRADIENT_NONFINITE)
     return h->err(ds.status, "OPT-001 rejects non-finite unscaled gradients");
+  if (ds.status == SLM_ERR_MODEL_GRADIENT_NORM_NONFINITE)
+    return h->err(ds.status, "OPT-001 global gradient norm is non-finite");
+  if (ds.status != SLM_OK) return h->err(SLM_ERR_INTERNAL, "unexpected clip check status");
+  const float tolerance = 0.05f;  // CLIP_VERIFICATION_TOLERANCE, trainer.rs:161
+  if (ds.clip_scale < 1.0f - tolerance) {
+    char msg[192];
+    std::snprintf(msg, sizeof(msg),
+                  "AdamW requires globally clipped FP32 gradients: update %llu re-measured a "
+                  "clip scale of %e, outside the 0.05 verification tolerance of 1.0",
+                  (unsigned long long)one_based_update, double(ds.clip_scale));
+    return h->err(SLM_ERR_P12_OPTIMIZER_GRADIENT_INVALID, msg);
   }
   // trainer.rs:262-273: u32 index, then the frozen schedule's exact lr bits.
   if (one_based_update > 0xffffffffull)

@@ -1153,6 +1153,108 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
                  fp, warp_sums);
 }
 
+// ---- the reference's sequential clip check (strict drop-in) ---------------------
+// CanonicalAdamw re-measures the clip of the gradients it is handed with
+// gradient_clip_scale (src/model/oracle.rs:486-507): `sum += g * g` in f32,
+// one element after another, then min(1 / sqrt(sum), 1).  At 135M terms that
+// sequential f32 sum drifts far from the exact one, and the drop-in must take
+// the same accept / reject decision, so it is reproduced exactly: one CTA,
+// lane 0 of warp 1 streams 16 KB tiles into shared memory with cp.async.bulk,
+// thread 0 adds them in order (each add waits for the previous one: about
+// 4 cycles per element, ~0.3 s at 135M).  Elements after the last whole tile
+// are read from global memory.  Waits are bounded as in the other pipelines.
+constexpr uint32_t kRefStages = 4;
+constexpr uint32_t kRefTile = 4096;  // floats per stage (16 KB)
+
+__global__ void __launch_bounds__(64, 1)
+    reference_clip_kernel(const float* __restrict__ g, uint64_t n, DeviceStepState* st) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* tiles = reinterpret_cast<float*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRefStages * kRefTile * sizeof(float));
+  uint64_t* empty = full + kRefStages;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kRefStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint64_t n_tiles = n / kRefTile;
+  bool ok = true;
+  uint64_t issued = 0;
+  if (threadIdx.x == 32) {
+    for (; issued < n_tiles; ++issued) {
+      const uint32_t s = uint32_t(issued % kRefStages);
+      if (issued >= kRefStages &&
+          !mbar_wait(&empty[s], uint32_t((issued / kRefStages) - 1u) & 1u)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&full[s], kRefTile * sizeof(float));
+      bulk_load(tiles + size_t(s) * kRefTile, g + issued * kRefTile, kRefTile * sizeof(float),
+                &full[s]);
+    }
+  } else if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    bool bad = false;
+    for (uint64_t j = 0; j < n_tiles; ++j) {
+      const uint32_t s = uint32_t(j % kRefStages);
+      if (!mbar_wait(&full[s], uint32_t(j / kRefStages) & 1u)) {
+        ok = false;
+        break;
+      }
+      const float4* t = reinterpret_cast<const float4*>(tiles + size_t(s) * kRefTile);
+#pragma unroll 4
+      for (uint32_t k = 0; k < kRefTile / 4; ++k) {
+        const float4 v = t[k];
+        bad |= !(finite_f32(v.x) && finite_f32(v.y) && finite_f32(v.z) && finite_f32(v.w));
+        sum = __fadd_rn(sum, __fmul_rn(v.x, v.x));
+        sum = __fadd_rn(sum, __fmul_rn(v.y, v.y));
+        sum = __fadd_rn(sum, __fmul_rn(v.z, v.z));
+        sum = __fadd_rn(sum, __fmul_rn(v.w, v.w));
+      }
+      mbar_arrive(&empty[s]);
+    }
+    if (ok) {
+      for (uint64_t i = n_tiles * kRefTile; i < n; ++i) {
+        const float x = g[i];
+        bad |= !finite_f32(x);
+        sum = __fadd_rn(sum, __fmul_rn(x, x));
+      }
+      float clip = 1.0f;
+      int32_t status = kStatusOk;
+      if (bad) {
+        status = kStatusGradientNonfinite;
+      } else if (!finite_f32(sum)) {
+        status = kStatusNormNonfinite;
+      } else if (sum != 0.0f) {
+        const float c = __fdiv_rn(1.0f, __fsqrt_rn(sum));
+        clip = c < 1.0f ? c : 1.0f;
+      }
+      st->sum_squares = double(sum);
+      st->grad_norm = double(__fsqrt_rn(sum));
+      st->clip_scale = clip;
+      st->clip_apply = 1.0f;  // the gradients arrive clipped
+      st->loss_scale_used = 1.0f;
+      st->next_loss_scale = 1.0f;
+      st->skipped = status == kStatusOk ? 0u : 1u;
+      st->nonfinite = status == kStatusOk ? 0u : 1u;
+      st->result_nonfinite = 0u;
+      st->rejected = 0u;
+      st->status = status;
+    }
+  }
+  // After an expired wait the producer waits (bounded) for its copies still
+  // in flight before the block exits.
+  if (__syncthreads_or(ok ? 0 : 1)) {
+    if (threadIdx.x == 32)
+      for (uint64_t u = issued > kRefStages ? issued - kRefStages : 0; u < issued; ++u)
+        mbar_wait(&full[u % kRefStages], uint32_t(u / kRefStages) & 1u);
+    if (threadIdx.x == 0) atomicOr(&st->kernel_error, 1u);
+  }
+}
+
 // ---- state initialisation / validation ----------------------------------------
 // bf16 weights -> f32 (the bits shifted into the high half, as the
 // reference's bf16_bits_to_f32 does for every parameter it reloads into the
@@ -1625,6 +1727,16 @@ cudaError_t launch_init_from_master(float* master, float* moment, float* varianc
   e = cudaMemsetAsync(variance, 0, n * sizeof(float), stream);
   if (e != cudaSuccess) return e;
   init_from_master_kernel<<<current_sms() * 8, 256, 0, stream>>>(master, w16, n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
+                                  cudaStream_t stream) {
+  const int bytes = int(kRefStages * kRefTile * sizeof(float) + 2 * kRefStages * sizeof(uint64_t));
+  cudaError_t e = cudaFuncSetAttribute(reference_clip_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  reference_clip_kernel<<<1, 64, bytes, stream>>>(g, n, st);
   return cudaGetLastError();
 }
 

@@ -95,6 +95,7 @@ struct __align__(16) DeviceStepState {
   uint32_t kernel_error;
   uint32_t reserved[3];
 };
+static_assert(sizeof(DeviceStepState) == 80, "DeviceStepState layout");
 
 // ZeRO-1 over peer memory: device addresses (mapped into this process with
 // CUDA IPC) of every rank's gradient buffer, gathered-partials area, flag
@@ -187,6 +188,11 @@ cudaError_t launch_accumulate_norm(int dtype, float* acc, const void* micro, uin
                                    const FinalizeParams& fp, cudaStream_t stream);
 // f32 copy of the bf16 weights (n elements, both 16-byte aligned).
 cudaError_t launch_export_f32(const uint16_t* w16, float* dst, uint64_t n, cudaStream_t stream);
+// The reference's own clip check for the strict drop-in: a sequential f32
+// sum of squares over g[0..n) (16-byte aligned), then min(1/sqrt(sum), 1);
+// fills st as the norm pass would for a static scale of 1 without clipping.
+cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
+                                  cudaStream_t stream);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

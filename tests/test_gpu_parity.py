@@ -407,6 +407,31 @@ def test_apply_update_rejections_match_reference(torch):
         assert_same_bits(got[key], state[key], key)
 
 
+def test_apply_update_accepts_the_production_width_clip_probe(torch):
+    # tests/p12_trainer.rs:406-446 at the canonical width: g_i = ((i % 977) - 488)
+    # * 1e-3, clipped once with the reference's own sequential f32 clip scale
+    # (oracle.rs:486-507).  The strict apply_update re-verifies the clip over
+    # the fixed tree, must accept it (tolerance 0.05), and update exactly like
+    # the oracle's strict apply.
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    n = table.parameter_count
+    g = ((np.arange(n) % 977).astype(np.float32) - np.float32(488.0)) * np.float32(1e-3)
+    st, scale = oracle.gradient_clip_scale(g)
+    assert st == oracle.OK and 0.0 < scale < 1.0
+    g = (g * np.float32(scale)).astype(np.float32)
+    state = synth.optimizer_state(n, 3)
+    lr = oracle.canonical_learning_rate(1)[1]
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        opt.apply_normalized_clipped_gradients(g, lr, 1, with_sha=False)
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in state.items()}
+    assert oracle.apply_normalized_clipped_gradients(g, lr, 1, table.offsets, table.decay,
+                                                     ost)[0] == oracle.OK
+    for key in ("master", "moment", "variance", "bf16"):
+        assert_same_bits(got[key], ost[key], key)
+
+
 def test_apply_update_matches_oracle_over_steps(torch):
     table = TensorTable.from_dimensions(GqaDimensions.oracle_fixture())
     n = table.parameter_count

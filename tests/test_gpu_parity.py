@@ -407,6 +407,51 @@ def test_apply_update_rejections_match_reference(torch):
         assert_same_bits(got[key], state[key], key)
 
 
+def test_reference_known_answers_on_the_device(torch):
+    # The reference's own optimizer KATs (src/model/oracle.rs:1464-1481, read as
+    # text into tests/golden/reference_kats.json), reproduced by the CUDA path:
+    # the AdamW step's moment / variance bits through the fused step, and the
+    # clip of [3, 4] / [0, 0] / NaN through the strict apply_update check.
+    import json
+    from pathlib import Path
+
+    kats = json.loads((Path(__file__).resolve().parent / "golden" /
+                       "reference_kats.json").read_text())["values"]
+    k = kats["adamw_step"]
+    table = TensorTable(names=("w.weight",), shapes=((1,),), elements=(1,), decay=(True,))
+    with B200Adamw(table) as opt:
+        th = np.array([k["theta"]], np.float32)
+        opt.load_state(th, np.array([k["moment"]], np.float32),
+                       np.array([k["variance"]], np.float32), synth.bf16_rne_bits(th))
+        opt.step(to_device(torch, np.array([k["gradient"]], np.float32)),
+                 StepOptions(learning_rate=k["learning_rate"], one_based_update=k["t"],
+                             decay_weight=k["weight_decay"], apply_clip=False))
+        got = opt.read_state()
+    assert int(got["moment"].view(np.uint32)[0]) == k["moment_bits"]
+    assert int(got["variance"].view(np.uint32)[0]) == k["variance_bits"]
+    assert got["master"][0] < k["master_below"]
+    assert int(got["bf16"][0]) == int(synth.bf16_rne_bits(got["master"])[0])
+
+    two = TensorTable(names=("a.weight", "b.weight"), shapes=((1,), (1,)), elements=(1, 1),
+                      decay=(True, True))
+    st = synth.optimizer_state(2, 0)
+    lr1 = oracle.canonical_learning_rate(1)[1]
+    with B200Adamw(two) as opt:
+        opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
+        with pytest.raises(SlmError) as e:  # clip [3, 4] = 0.2: rejected, 0.2 reported
+            opt.apply_normalized_clipped_gradients(
+                np.array(kats["clip_3_4"]["input"], np.float32), lr1, 1, with_sha=False)
+        assert e.value.code == "P12_OPTIMIZER_GRADIENT_INVALID"
+        assert f"{float(np.float32(kats['clip_3_4']['expected_f32'])):e}" in e.value.message
+        with pytest.raises(SlmError) as e:
+            opt.apply_normalized_clipped_gradients(
+                np.array([np.nan, 1.0], np.float32), lr1, 1, with_sha=False)
+        assert e.value.code == kats["clip_nan"]["expected_code"]
+        # [0, 0] re-verifies at exactly 1.0 and is applied
+        opt.apply_normalized_clipped_gradients(
+            np.array(kats["clip_zero"]["input"], np.float32), lr1, 1, with_sha=False)
+
+
 def test_apply_update_accepts_the_production_width_clip_probe(torch):
     # tests/p12_trainer.rs:406-446 at the canonical width: g_i = ((i % 977) - 488)
     # * 1e-3, clipped once with the reference's own sequential f32 clip scale

@@ -4,14 +4,23 @@
 // bound by HBM bandwidth: 128-bit coalesced loads/stores, streaming cache
 // hints for the state that is touched once, f64 shuffle trees for the norm.
 //
-//   norm_partials_kernel  -- reads the gradient once, unscales, forms one f64
-//                            partial per 65,536-element chunk with the fixed
-//                            tree, flags non-finite values; its last block
-//                            (atomic completion counter, no spinning) reduces
-//                            the partials, computes the clip and the skip
-//                            decision and advances the dynamic loss scaler.
-//   adamw_update_kernel   -- persistent grid over 4,096-element tiles: unscale,
-//                            clip, AdamW (fp32 master/m/v), bf16 weight copy.
+//   norm_bulk_kernel         -- (default; norm_partials_kernel is the per-chunk
+//                               form) reads the gradient once, unscales, forms
+//                               one f64 partial per 65,536-element chunk with
+//                               the fixed tree, flags non-finite values; its
+//                               last block (atomic completion counter, no
+//                               spinning) reduces the partials, computes the
+//                               clip and the skip decision and advances the
+//                               dynamic loss scaler.
+//   adamw_update_bulk_kernel -- (default; adamw_update_kernel is the
+//                               register-staged form) persistent grid over
+//                               2,048-element tiles streamed through shared
+//                               memory: unscale, clip, AdamW (fp32 master/m/v),
+//                               bf16 weight copy (also to every peer in ZeRO-1).
+//   accumulate*, zero1_*, peer_barrier_kernel, reference_clip_kernel,
+//   export_f32_kernel, init / validate -- micro-batch sums, the ZeRO-1
+//                               exchange, the strict drop-in's clip check, the
+//                               f32 weight export and state set-up.
 //
 // Exactness: every f32 operation of the AdamW recurrence is an explicit
 // round-to-nearest intrinsic (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn), so

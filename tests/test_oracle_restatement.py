@@ -248,3 +248,18 @@ def test_multithreaded_step_equals_single_threaded():
     assert r1.sum_squares == r8.sum_squares
     for k in s1:
         assert np.array_equal(s1[k], s8[k])
+
+
+@pytest.mark.parametrize("n", [1, 2, 977, 20_000])
+def test_reference_sequential_clip_matches_python_restatement(n):
+    # src/model/oracle.rs:486-507: `sum += g * g` in f32, one element after
+    # another, then min(1 / sqrt(sum), 1) -- restated here element by element
+    # with numpy float32 scalars (one rounding per operation).
+    g = (((np.arange(n) % 977).astype(np.float32) - F(488.0)) * F(1e-3)).astype(np.float32)
+    total = F(0.0)
+    for x in g:
+        total = F(total + F(x * x))
+    expect = F(1.0) if total == 0 else min(F(F(1.0) / F(np.sqrt(total))), F(1.0))
+    st, got = oracle.gradient_clip_scale(g)
+    assert st == oracle.OK
+    assert F(got).view(np.uint32) == expect.view(np.uint32)

@@ -26,13 +26,14 @@ def np_powi(base: float, exponent: int) -> np.float32:
     b = F(base)
     r = F(1.0)
     e = exponent
-    while True:
-        if e & 1:
-            r = F(r * b)
-        e >>= 1
-        if e == 0:
-            break
-        b = F(b * b)
+    with np.errstate(over="ignore"):  # 1.5^t overflows to inf, as in f32
+        while True:
+            if e & 1:
+                r = F(r * b)
+            e >>= 1
+            if e == 0:
+                break
+            b = F(b * b)
     return r
 
 

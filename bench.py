@@ -21,6 +21,16 @@ the public C ABI with the gradients in pinned host memory (H2D copy and the
 D2H result read inside the timed region).  ``--impl reference`` times the CPU
 oracle -- the restatement of the reference's Rust scalar step (the reference
 itself cannot be built here) -- on all host cores.
+
+After the timed region every arm re-runs one step from the seeded state and
+compares the resulting state hash, norm, clip and loss scale with the values
+the oracle produced for the same inputs (``tests/golden/step_golden.json``,
+written by ``tests/golden/make_step_golden.py``), plus one step with an
+injected +inf that must be skipped; the line carries the outcome as
+``parity`` and the run exits non-zero on a mismatch.
+
+``--nvlink-peak`` (one process, ``--gpus N`` devices) measures the peer-copy
+bandwidth the ZeRO-1 roofline is quoted against instead of benchmarking.
 """
 from __future__ import annotations
 
@@ -45,9 +55,12 @@ FALLBACK_HBM_GBS = 6650.0
 UPDATE_BYTES = {"mixed": 28, "fp32": 30}
 STEP_BYTES = {"mixed": 30, "fp32": 34}  # + the norm pass's read of g
 # dram__bytes_read.sum + dram__bytes_write.sum of one full-size update-kernel
-# launch (135,285,504 params, one-pass ncu capture, cold cache); None where no
-# capture exists.
-UPDATE_TRAFFIC_BYTES = {"mixed": 3.725e9, "fp32": None}
+# launch (135,285,504 params, one-pass ncu capture, cold cache), from
+# profiles/step_kernels_traffic_135m_mixed.md and
+# profiles/step_kernels_traffic_135m_fp32.md.
+UPDATE_TRAFFIC_BYTES = {"mixed": 3.725e9, "fp32": 3.996e9}
+GOLDEN = ROOT / "tests" / "golden" / "step_golden.json"
+INF_SEED = 5  # seed of the injected +inf in the skip check (make_step_golden.py)
 
 
 def parse_args():
@@ -64,6 +77,10 @@ def parse_args():
     ap.add_argument("--params", type=int, default=0,
                     help="profiling only: run on the first N parameters (whole 65,536-element "
                          "chunks) of the 135M layout instead of all of it")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="profiling only: skip the post-run check against the golden step")
+    ap.add_argument("--nvlink-peak", action="store_true",
+                    help="measure peer-copy bandwidth over --gpus devices and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -187,6 +204,186 @@ def gpu_smi_id(device: int) -> str:
         return str(device)
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for every CPU number."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def load_golden() -> dict | None:
+    try:
+        return json.loads(GOLDEN.read_text())
+    except Exception:
+        return None
+
+
+def f32_bits(x: float) -> int:
+    import struct
+
+    return struct.unpack("<I", struct.pack("<f", float(x)))[0]
+
+
+def compare_step(res, sha: str, want: dict) -> dict:
+    """One step's outcome against a golden record (bit-level comparisons)."""
+    out = {"state_bit_exact": sha == want["sha256"],
+           "sum_squares_equal": float(res.sum_squares).hex() == want["sum_squares_hex"],
+           "clip_equal": f32_bits(res.clip_scale) == want["clip_scale_bits"],
+           "skipped_equal": int(res.skipped) == want["skipped"],
+           "next_loss_scale_equal": float(res.next_loss_scale) == want["next_loss_scale"]}
+    out["ok"] = all(out.values())
+    return out
+
+
+def single_parity(opt, table, state, host_grads, dev_grads, opts, workload: str) -> dict:
+    """Post-run check of the single-GPU step: from the seeded state, one step
+    on the benchmark's gradients and one on a copy carrying an injected +inf,
+    each compared with the oracle's outcome in tests/golden/step_golden.json."""
+    import torch
+
+    from slmopt import synth
+
+    g = load_golden()
+    P = table.parameter_count
+    if g is None or g.get("params") != P:
+        return {"checked": False, "reason": "no golden record for this parameter count"}
+    opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
+                   validate=False)
+    opt.set_loss_scale(65536.0)
+    res = opt.step(dev_grads, opts)
+    out = {"checked": True, "case": workload, "against": "tests/golden/step_golden.json"}
+    out["step"] = compare_step(res, opt.state_sha256(), g[workload])
+    ok = out["step"]["ok"]
+    if workload == "mixed":
+        bad = host_grads.copy()
+        synth.inject_nonfinite(bad, INF_SEED, table.offsets)
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
+                       validate=False)
+        opt.set_loss_scale(65536.0)
+        res = opt.step(torch.from_numpy(bad).cuda(), opts)
+        out["skip"] = compare_step(res, opt.state_sha256(), g["skip"]["1"])
+        ok = ok and out["skip"]["ok"]
+    out["bit_exact"] = ok
+    return out
+
+
+def time_apply_update(table, state, calls: int = 2) -> dict:
+    """The strict drop-in (slm_opt_apply_update, the reference's apply_update
+    contract) at full size: host f32 gradients already clipped (norm 0.9),
+    the reference's sequential clip re-check on the device, AdamW, no hash.
+    Wall clock per call (the call is synchronous) and the device time of its
+    three phases (upload, sequential clip check, update) from the handle's
+    phase timer."""
+    import numpy as np
+    import torch
+
+    from slmopt import B200Adamw, _lib, synth
+
+    P = table.parameter_count
+    g = synth.grads_f32(P, 0)
+    g *= np.float32(0.9 / float(np.sqrt(np.sum(g.astype(np.float64) ** 2))))
+    lib = _lib.load()
+    times = []
+    with B200Adamw(table, device=0) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
+                       validate=False)
+        for t in range(1, calls + 2):
+            if t == 2:
+                opt.phase_timing(True)  # after the first call, which allocates staging
+            lr = ctypes_lr(lib, t)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            opt.apply_normalized_clipped_gradients(g, lr, t, 0, with_sha=False)
+            times.append((time.perf_counter() - t0) * 1e3)
+        phases, n = opt.phase_times()
+        opt.phase_timing(False)
+    times = times[1:]
+    return {"api": "slm_opt_apply_update", "params": P, "calls": len(times),
+            "ms_per_call": statistics.median(times),
+            "phases_ms": phases, "phase_calls": n,
+            "note": "synchronous wall clock; host f32 gradients (pageable), the reference's "
+                    "sequential f32 clip re-verification on the device, AdamW; state hash off"}
+
+
+def ctypes_lr(lib, t: int) -> float:
+    import ctypes
+
+    out = ctypes.c_float()
+    lib.slm_canonical_learning_rate(ctypes.c_uint64(t), ctypes.byref(out))
+    return out.value
+
+
+def run_nvlink_peak(args) -> None:
+    """Peer-copy bandwidth between this box's GPUs (copy engines, CUDA events).
+
+    * one direction: 1 GiB from GPU 0 to GPU 1;
+    * both directions at once: 1 GiB 0 -> 1 and 1 GiB 1 -> 0 on two streams;
+    * all-to-all over N GPUs: every GPU pulls a 256 MiB slice from each of the
+      other N-1 at once (one stream per pair), the ZeRO-1 gradient exchange's
+      pattern; per-GPU inbound bandwidth.
+    Best of 5 repetitions each; GB/s = 1e9 bytes/s."""
+    import torch
+
+    n = min(args.gpus, torch.cuda.device_count())
+    if n < 2:
+        raise SystemExit("--nvlink-peak needs --gpus >= 2 and as many visible GPUs")
+    devs = list(range(n))
+    for a in devs:
+        for b in devs:
+            if a != b and not torch.cuda.can_device_access_peer(a, b):
+                raise SystemExit(f"GPU {a} cannot access GPU {b}")
+
+    def timed(pairs, nbytes, reps=5):
+        # pairs: list of (src_dev, dst_dev); one stream per pair on the destination
+        bufs = []
+        for s, d in pairs:
+            src = torch.empty(nbytes, dtype=torch.uint8, device=s)
+            dst = torch.empty(nbytes, dtype=torch.uint8, device=d)
+            bufs.append((src, dst, torch.cuda.Stream(device=d)))
+        for src, dst, st in bufs:  # warm up (enables peer access)
+            with torch.cuda.device(dst.device), torch.cuda.stream(st):
+                dst.copy_(src, non_blocking=True)
+        for d in devs:
+            torch.cuda.synchronize(d)
+        best = None
+        for _ in range(reps):
+            evs = []
+            for src, dst, st in bufs:
+                with torch.cuda.device(dst.device):
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    with torch.cuda.stream(st):
+                        dst.copy_(src, non_blocking=True)
+                    e1.record(st)
+                    evs.append((e0, e1))
+            for d in devs:
+                torch.cuda.synchronize(d)
+            ms = max(e0.elapsed_time(e1) for e0, e1 in evs)
+            best = ms if best is None else min(best, ms)
+        del bufs
+        return best
+
+    gib = 1 << 30
+    one = timed([(0, 1)], gib)
+    both = timed([(0, 1), (1, 0)], gib)
+    out = {"what": "peer copy bandwidth (cudaMemcpyAsync between devices, copy engines)",
+           "gpus": n, "gpu_name": torch.cuda.get_device_name(0),
+           "one_direction_gbs": gib / (one * 1e-3) / 1e9,
+           "both_directions_gbs_per_direction": gib / (both * 1e-3) / 1e9}
+    if n > 2:
+        sl = 256 << 20
+        pairs = [(q, d) for d in devs for q in devs if q != d]
+        ms = timed(pairs, sl, reps=3)
+        out["all_to_all_inbound_gbs_per_gpu"] = (n - 1) * sl / (ms * 1e-3) / 1e9
+        out["all_to_all_slice_bytes"] = sl
+    print(json.dumps(out), flush=True)
+
+
 def cpu_baseline_sample(table, state, grads, workload: str, seconds: float = 12.0) -> dict:
     """The oracle (CPU port of the reference's step) on the host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -207,7 +404,8 @@ def cpu_baseline_sample(table, state, grads, workload: str, seconds: float = 12.
     oracle.step(cfg, grads, table.offsets, table.decay, st, threads=1)
     single = time.perf_counter() - t0
     med = statistics.median(times)
-    return {"value": P / med, "unit": UNIT, "cores": cores, "kind": "port",
+    return {"value": P / med, "unit": UNIT, "cores": cores, "cpu_model": cpu_model(),
+            "kind": "port",
             "sample": f"{len(times)} full {P:,}-param steps ({workload}) with {cores} threads, "
                       f"median {med * 1e3:.1f} ms",
             "ms_per_step": med * 1e3,
@@ -241,13 +439,16 @@ def run_reference(args) -> None:
     oracle.step(cfg, g, off, [1], st, threads=cores)
     rate = probe / (time.perf_counter() - t0)
     per_step = 90.0 / (args.steps + args.warmup)
-    n = int(min(P, max(16 * 65536, rate * per_step)) // 65536 * 65536)
-    n = min(n, P)
-    offsets = table.offsets
-    k_end = int(np.searchsorted(offsets, n, side="right"))
-    off = np.concatenate([offsets[:k_end], [n]]).astype(np.uint64)
-    off = np.unique(off)
-    decay = list(table.decay[: len(off) - 1])
+    if rate * per_step >= P:  # the whole step fits the time budget
+        n = P
+        off = np.asarray(table.offsets, dtype=np.uint64)
+        decay = list(table.decay)
+    else:
+        n = int(max(16 * 65536, rate * per_step) // 65536 * 65536)
+        offsets = table.offsets
+        k_end = int(np.searchsorted(offsets, n, side="right"))
+        off = np.unique(np.concatenate([offsets[:k_end], [n]]).astype(np.uint64))
+        decay = list(table.decay[: len(off) - 1])
     st = synth.optimizer_state(n, 0)
     g = synth.grads_bf16(n, 0) if args.workload == "mixed" else synth.grads_f32(n, 0)
     for _ in range(args.warmup):
@@ -257,7 +458,8 @@ def run_reference(args) -> None:
         oracle.step(cfg, g, off, decay, st, threads=cores)
     dt = time.perf_counter() - t0
     value = n * args.steps / dt
-    sample = (f"first {n:,} of {P:,} params (whole 65,536-element chunks of the PARAM-001 "
+    sample = (f"all {P:,} params per step, {cores} threads" if n == P else
+              f"first {n:,} of {P:,} params (whole 65,536-element chunks of the PARAM-001 "
               f"flat buffer) per step, {cores} threads")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -266,8 +468,8 @@ def run_reference(args) -> None:
         "data": "synthetic (seeded numpy Philox normals)",
         "config": workload_config(args, world, P, len(table)),
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "cpu_model": cpu_model(),
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -392,15 +594,25 @@ def run_single(args) -> None:
         "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale,
                    "loss_scale": res.loss_scale_used},
     }
+    full = P == TensorTable.from_dimensions(GqaDimensions.canonical()).parameter_count
+    if not args.no_parity:
+        line["parity"] = single_parity(opt, table, state, grads, dev_grads, opts, args.workload)
+    opt.close()
+    if full and not args.no_parity:
+        line["apply_update"] = time_apply_update(table, state)
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(table, state, grads, args.workload)
-    opt.close()
     print(json.dumps(line), flush=True)
+    if "parity" in line and line["parity"].get("checked") and not line["parity"]["bit_exact"]:
+        raise SystemExit("parity check against the oracle's golden step FAILED")
 
 
 def main():
     args = parse_args()
     rank, world, _ = dist_env()
+    if args.nvlink_peak:
+        run_nvlink_peak(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -222,11 +222,14 @@ int slm_opt_export_weights_f32(slm_opt_handle* h, float* dst_device, uint64_t n,
  * phase durations in ms, the phase count and the number of steps timed;
  * slm_opt_phase_name names phase i for this handle's mode (NULL past the end):
  *   one GPU:         norm pass, update
- *   ZeRO-1 peer:     gradient barrier, peer reduce, finalize,
- *                    update + weight stores, weight barrier
+ *   ZeRO-1 peer:     gradient barrier + peer reduce,
+ *                    finalize + update + weight stores + weight barrier
  *   ZeRO-1 NCCL:     gradient all-to-all, reduce, partials all-gather,
  *                    finalize, update, weight all-gather
- * A host gradient's upload is not part of any phase. */
+ *   slm_opt_apply_update: gradient upload, sequential clip check, update
+ * A host gradient's upload is not part of any slm_opt_step phase.  The sums
+ * describe one entry point: a timed call of the other (slm_opt_step versus
+ * slm_opt_apply_update) starts them afresh. */
 int slm_opt_phase_timing(slm_opt_handle* h, int enable);
 int slm_opt_phase_times(slm_opt_handle* h, double* mean_ms, uint32_t capacity,
                         uint32_t* n_phases, uint64_t* steps);
@@ -342,10 +345,13 @@ int slm_opt_gradient_buffer(slm_opt_handle* h, void** out_device_ptr, uint64_t* 
  * Its scratch is a fixed file-scope device array (about 33 KB on every GPU that
  * loads the library, held until exit), so nothing is allocated; n above
  * SLM_NOALLOC_MAX_ELEMENTS is rejected with SLM_ERR_SIZE_LIMIT.  The result is
- * written to the caller's device memory `out_device`, stream-ordered on
- * `stream`.  The first call on a device looks up the array's device address,
- * so make that first call before any stream capture.  All calls on a device
- * share the array: calls whose work overlaps on the GPU race. */
+ * written to the caller's device memory `out_device` (8-byte aligned),
+ * stream-ordered on `stream`; `grads` must be aligned to its element size.
+ * The first call on a device looks up the array's device address and caches
+ * it, so make that first call before any stream capture, and do not call this
+ * entry point on a device after cudaDeviceReset (the reset unloads the array).
+ * All calls on a device share the array: calls whose work overlaps on the GPU
+ * race. */
 #define SLM_NOALLOC_MAX_ELEMENTS 268435456ull /* 2^28 elements = 4,096 chunks */
 typedef struct slm_norm_result {
     double sum_squares;  /* fixed-tree f64 sum of (g / loss_scale)^2 */

@@ -278,6 +278,11 @@ int phase_harvest(slm_opt_handle* h) {
   if (n < 2) return SLM_OK;
   int st = h->cuda(cudaEventSynchronize(t.ev[n - 1]), "phase timing");
   if (st) return st;
+  if (t.finished_kind != t.kind) {  // another entry point's phases: start the sums afresh
+    for (double& a : t.acc) a = 0.0;
+    t.steps = 0;
+    t.kind = t.finished_kind;
+  }
   for (int i = 0; i + 1 < n; ++i) {
     float ms = 0.0f;
     if ((st = h->cuda(cudaEventElapsedTime(&ms, t.ev[i], t.ev[i + 1]), "phase timing")))
@@ -328,10 +333,11 @@ int slmopt::phase_mark(slm_opt_handle* h, cudaStream_t s) {
   return h->cuda(cudaEventRecord(t.ev[t.marks++], s), "phase timing");
 }
 
-void slmopt::phase_end(slm_opt_handle* h) {
+void slmopt::phase_end(slm_opt_handle* h, int kind) {
   PhaseTimer& t = h->timer;
   if (!t.enabled) return;
   t.finished = t.marks;
+  t.finished_kind = kind;
   t.marks = 0;
 }
 
@@ -836,6 +842,7 @@ int slm_opt_phase_timing(slm_opt_handle* h, int enable) {
   t.finished = 0;
   t.steps = 0;
   t.phases = 0;
+  t.kind = t.finished_kind = kStepCall;
   for (double& a : t.acc) a = 0.0;
   return SLM_OK;
 }
@@ -856,13 +863,15 @@ int slm_opt_phase_times(slm_opt_handle* h, double* mean_ms, uint32_t capacity,
 
 const char* slm_opt_phase_name(const slm_opt_handle* h, uint32_t phase) {
   static const char* const kSingle[] = {"norm pass", "update"};
-  static const char* const kPeer[] = {"gradient barrier", "peer reduce", "finalize",
-                                      "update + weight stores", "weight barrier"};
+  static const char* const kApply[] = {"gradient upload", "sequential clip check", "update"};
+  static const char* const kPeer[] = {"gradient barrier + peer reduce",
+                                      "finalize + update + weight stores + weight barrier"};
   static const char* const kNccl[] = {"gradient all-to-all", "reduce", "partials all-gather",
                                       "finalize", "update", "weight all-gather"};
   if (!h) return nullptr;
+  if (h->timer.kind == kApplyUpdateCall) return phase < 3 ? kApply[phase] : nullptr;
   if (!h->sharded()) return phase < 2 ? kSingle[phase] : nullptr;
-  if (h->exchange == SLM_ZERO1_PEER) return phase < 5 ? kPeer[phase] : nullptr;
+  if (h->exchange == SLM_ZERO1_PEER) return phase < 2 ? kPeer[phase] : nullptr;
   return phase < 6 ? kNccl[phase] : nullptr;
 }
 
@@ -898,14 +907,17 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   DeviceGuard guard(h->device);
   cudaStream_t s = nullptr;
   const void* dev = nullptr;
-  int st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev);
+  int st = phase_begin(h, s);
   if (st) return st;
+  if ((st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev))) return st;
+  if ((st = phase_mark(h, s))) return st;
   // Re-verification first (trainer.rs:250-260), with the reference's own
   // sequential f32 clip scale so that the accept / reject decision is the
   // reference's; nothing is written on failure.
   if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s),
                     "clip check kernel")))
     return st;
+  if ((st = phase_mark(h, s))) return st;
   DeviceStepState ds;
   if ((st = read_state(h, s, &ds))) return st;
   if (ds.kernel_error) return h->err(SLM_ERR_INTERNAL, "the clip check's copy pipeline stalled");
@@ -936,6 +948,8 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   cfg.learning_rate = learning_rate;
   cfg.one_based_update = uint32_t(one_based_update);
   if ((st = enqueue_update(h, dev, SLM_DTYPE_F32, &cfg, s))) return st;
+  if ((st = phase_mark(h, s))) return st;
+  phase_end(h, kApplyUpdateCall);
   if ((st = read_state(h, s, &ds))) return st;
   if (ds.result_nonfinite)
     return h->err(SLM_ERR_MODEL_OPTIMIZER_RESULT_NONFINITE, "OPT-001 produced non-finite state");

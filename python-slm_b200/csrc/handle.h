@@ -62,7 +62,13 @@ struct PhaseTimer {
   double acc[kMaxMarks - 1] = {};
   uint64_t steps = 0;
   uint32_t phases = 0;
+  // Which entry point the sums describe (kStepCall, kApplyUpdateCall): a call
+  // of the other kind restarts them, so the phase names always fit the sums.
+  int kind = 0;
+  int finished_kind = 0;
 };
+constexpr int kStepCall = 0;
+constexpr int kApplyUpdateCall = 1;
 }  // namespace slmopt
 
 struct slm_opt_handle {
@@ -133,6 +139,7 @@ struct slm_opt_handle {
   void* d_gradbuf = nullptr;       // registered gradient buffer, P * 4 bytes, exported
   uint32_t* d_flags = nullptr;     // kFlagSlots * kMaxRanks arrival epochs, exported
   slmopt::PeerTable peers{};       // every rank's buffers as mapped here (own included)
+  int grid_peer_update = 0;        // persistent grid of the peer-exchange update kernel
   void* opened[slmopt::kMaxRanks][4] = {};  // IPC mappings to close on destroy
   uint32_t epoch = 0;              // step counter shared (implicitly) by all ranks
   slmopt::PhaseTimer timer;
@@ -156,7 +163,7 @@ namespace slmopt {
 // marks the step complete.  No-ops unless timing is enabled.
 int phase_begin(slm_opt_handle* h, cudaStream_t s);
 int phase_mark(slm_opt_handle* h, cudaStream_t s);
-void phase_end(slm_opt_handle* h);
+void phase_end(slm_opt_handle* h, int kind = kStepCall);
 // Allocates the per-handle device state for [shard_begin, shard_begin+shard_len)
 // with the bf16 buffer sized w16_elems; used by both create paths (api.cu).
 int allocate_state(slm_opt_handle* h, uint64_t w16_elems);

@@ -233,79 +233,115 @@ struct PartialsView {
   }
 };
 
+// Thread t's share of the finalize tree: partials t, t+256, ... added in that
+// order; up to 8 of its loads go out together (2,065 partials at 135M: one
+// round trip instead of 9).
+__device__ __forceinline__ double finalize_lane_sum(const PartialsView& partials,
+                                                   uint32_t total_chunks, uint32_t t) {
+  double v = 0.0;
+  for (uint32_t c0 = t; c0 < total_chunks; c0 += 8 * kTreeThreads) {
+    double q[8];
+#pragma unroll
+    for (uint32_t b = 0; b < 8; ++b) {
+      const uint32_t c = c0 + b * kTreeThreads;
+      q[b] = c < total_chunks ? partials(c) : 0.0;
+    }
+#pragma unroll
+    for (uint32_t b = 0; b < 8; ++b)
+      if (c0 + b * kTreeThreads < total_chunks) v = __dadd_rn(v, q[b]);
+  }
+  return v;
+}
+
+// The step's decision from the reduced sum: clip, skip / reject, and the
+// dynamic scaler's next state.
+struct StepDecision {
+  float clip;        // min(max_norm / sqrtf((float)sum), 1); 1 for a zero sum; 0 if non-finite
+  float clip_apply;  // what the update multiplies by
+  float next_scale;
+  uint32_t good;
+  uint32_t skipped, rejected;
+  int32_t status;
+};
+
+__device__ __forceinline__ StepDecision decide_step(double sum, uint32_t nonfinite, float scale,
+                                                    uint32_t good_in, const FinalizeParams& fp) {
+  StepDecision d;
+  const float sumf = __double2float_rn(sum);
+  const bool norm_bad = !finite_f32(sumf);
+  if (norm_bad) {
+    d.clip = 0.0f;
+  } else if (sumf == 0.0f) {
+    d.clip = 1.0f;
+  } else {
+    d.clip = __fdiv_rn(fp.max_grad_norm, __fsqrt_rn(sumf));
+    d.clip = d.clip < 1.0f ? d.clip : 1.0f;
+  }
+  d.clip_apply = fp.apply_clip ? d.clip : 1.0f;
+  d.skipped = 0u;
+  d.rejected = 0u;
+  d.status = kStatusOk;
+  d.next_scale = scale;
+  d.good = fp.dynamic ? good_in : 0u;
+  if (nonfinite || norm_bad) {
+    d.skipped = 1u;
+    if (fp.nonfinite_policy == 1)
+      d.status = nonfinite ? kStatusGradientNonfinite : kStatusNormNonfinite;
+    if (fp.dynamic) {
+      d.next_scale = __fmul_rn(scale, 0.5f);
+      d.good = 0u;
+    }
+  } else if (fp.min_clip_accept > 0.0f && d.clip < fp.min_clip_accept) {
+    d.skipped = 1u;
+    d.rejected = 1u;
+    d.status = kStatusGradientInvalid;
+  } else if (fp.dynamic) {
+    d.good += 1u;
+    if (d.good >= fp.growth_interval) {
+      d.next_scale = __fmul_rn(scale, 2.0f);
+      d.good = 0u;
+    }
+  }
+  return d;
+}
+
+// Publishes a decision: the step record and, for a dynamic scale, the scaler.
+// result_nonfinite is left alone: the update kernels raise it, and it is
+// cleared before they start.
+__device__ __forceinline__ void write_decision(const StepDecision& d, double sum, uint32_t nonfinite,
+                                               float scale, DeviceStepState* st,
+                                               DeviceScaler* scaler, const FinalizeParams& fp) {
+  st->sum_squares = sum;
+  st->grad_norm = __dsqrt_rn(sum);
+  st->clip_scale = d.clip;
+  st->clip_apply = d.clip_apply;
+  st->loss_scale_used = scale;
+  st->nonfinite = nonfinite;
+  st->rejected = d.rejected;
+  st->skipped = d.skipped;
+  st->status = d.status;
+  if (fp.dynamic) {
+    scaler->scale = d.next_scale;
+    scaler->good_steps = d.good;
+  }
+  st->next_loss_scale = d.next_scale;
+  st->good_steps = d.good;
+}
+
 // Reduce the partials with the fixed tree, decide clip / skip, advance the
 // scaler.  Called by one whole 256-thread block; `nonfinite` is read from
 // thread 0 only.
 __device__ __forceinline__ void finalize_block(const PartialsView& partials, uint32_t nonfinite,
                                DeviceStepState* st, DeviceScaler* scaler,
                                const FinalizeParams& fp, double* warp_sums) {
-  // Thread t adds partials t, t+256, ... in that order; up to 8 of its loads
-  // go out together (2,065 partials at 135M: one round trip instead of 9).
-  double v = 0.0;
-  for (uint32_t c0 = threadIdx.x; c0 < fp.total_chunks; c0 += 8 * kTreeThreads) {
-    double q[8];
-#pragma unroll
-    for (uint32_t b = 0; b < 8; ++b) {
-      const uint32_t c = c0 + b * kTreeThreads;
-      q[b] = c < fp.total_chunks ? partials(c) : 0.0;
-    }
-#pragma unroll
-    for (uint32_t b = 0; b < 8; ++b)
-      if (c0 + b * kTreeThreads < fp.total_chunks) v = __dadd_rn(v, q[b]);
-  }
-  const double sum = block_fold(v, warp_sums);
+  const double sum = block_fold(finalize_lane_sum(partials, fp.total_chunks, threadIdx.x),
+                                warp_sums);
   if (threadIdx.x != 0) return;
-
   const float scale = fp.dynamic ? scaler->scale : fp.static_scale;
-  const float sumf = __double2float_rn(sum);
-  const bool norm_bad = !finite_f32(sumf);
-  float clip;
-  if (norm_bad) {
-    clip = 0.0f;
-  } else if (sumf == 0.0f) {
-    clip = 1.0f;
-  } else {
-    clip = __fdiv_rn(fp.max_grad_norm, __fsqrt_rn(sumf));
-    clip = clip < 1.0f ? clip : 1.0f;
-  }
-  st->sum_squares = sum;
-  st->grad_norm = __dsqrt_rn(sum);
-  st->clip_scale = clip;
-  st->clip_apply = fp.apply_clip ? clip : 1.0f;
-  st->loss_scale_used = scale;
-  st->nonfinite = nonfinite;
-  st->result_nonfinite = 0u;
-  st->rejected = 0u;
-  st->skipped = 0u;
-  st->status = kStatusOk;
-
-  float next = scale;
-  uint32_t good = fp.dynamic ? scaler->good_steps : 0u;
-  if (nonfinite || norm_bad) {
-    st->skipped = 1u;
-    if (fp.nonfinite_policy == 1)
-      st->status = nonfinite ? kStatusGradientNonfinite : kStatusNormNonfinite;
-    if (fp.dynamic) {
-      next = __fmul_rn(scale, 0.5f);
-      good = 0u;
-    }
-  } else if (fp.min_clip_accept > 0.0f && clip < fp.min_clip_accept) {
-    st->skipped = 1u;
-    st->rejected = 1u;
-    st->status = kStatusGradientInvalid;
-  } else if (fp.dynamic) {
-    good += 1u;
-    if (good >= fp.growth_interval) {
-      next = __fmul_rn(scale, 2.0f);
-      good = 0u;
-    }
-  }
-  if (fp.dynamic) {
-    scaler->scale = next;
-    scaler->good_steps = good;
-  }
-  st->next_loss_scale = next;
-  st->good_steps = good;
+  const StepDecision d =
+      decide_step(sum, nonfinite, scale, fp.dynamic ? scaler->good_steps : 0u, fp);
+  write_decision(d, sum, nonfinite, scale, st, scaler, fp);
+  st->result_nonfinite = 0u;  // the update pass runs after this kernel
   st->blocks_done = 0u;
   __threadfence();
 }
@@ -1304,79 +1340,112 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
   if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(bad_flag, 1u);
 }
 
-// ---- ZeRO-1 over peer memory ------------------------------------------------------
-// Flag barrier between the ranks of one node: lane q announces this rank's
-// arrival (the step's epoch) in rank q's flag array, then waits until rank q
-// has announced itself here.  Epochs only grow, so flags are never reset; the
-// wait is bounded and records kernel_error instead of hanging.  Once a wait of
-// this step has given up, later barriers of the step only announce: the step
-// has failed here, and a peer still inside it fails at its own bounded wait.
-__global__ void peer_barrier_kernel(PeerTable pt, int rank, int world, uint32_t slot,
-                                    uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns) {
-  const int q = threadIdx.x;
-  const bool failed = st->kernel_error != 0u;  // written by earlier kernels of this stream
-  __threadfence_system();
-  if (q < world)
-    *reinterpret_cast<volatile uint32_t*>(pt.flags[q] + slot * kMaxRanks + rank) = epoch;
-  if (q < world && !failed) {
-    const volatile uint32_t* mine = pt.flags[rank] + slot * kMaxRanks + q;
-    const uint64_t t0 = global_ns();
-    while (static_cast<int32_t>(*mine - epoch) < 0) {
-      if (global_ns() - t0 > timeout_ns) {
-        atomicOr(&st->kernel_error, 2u);
-        break;
-      }
-    }
-  }
-  __threadfence_system();
+// ---- ZeRO-1 over peer memory: two kernels per step ---------------------------------
+// zero1_peer_reduce_kernel: one block per chunk of this rank's shard.  Its
+// prologue is the gradient barrier (every block announces this rank's epoch to
+// every rank and waits, bounded, for every rank's announcement).  Then the
+// chunk streams through kPeerStages shared-memory stages: thread 0 issues, per
+// stage, one bulk copy (cp.async.bulk, no multicast) of `rows` tree rows from
+// every rank's gradient buffer -- over NVLink for the peers -- so the bytes in
+// flight cost no registers; the 256 threads add their 8-element vectors in
+// rank order 0..N-1 in f32, store the sums for the update, and accumulate the
+// unscaled squares in the single-replica tree order.  The chunk partial goes
+// straight into every rank's gathered area; the last block appends the
+// non-finite flag and raises every rank's partials flag.
+// zero1_peer_update_kernel: the bulk-copy update with the finalize in its
+// prologue (every block reduces all ranks' partials with the same tree, so
+// every block and every rank takes the same decision; block 0 publishes it)
+// and the weight barrier in its epilogue (the last block to finish announces
+// this rank's weights and waits, bounded, for every rank's).
+// Every wait is bounded by timeout_ns; after a wait of a step has given up
+// (kernel_error), later waits of the step return at once.
+constexpr uint32_t kPeerStages = 3;
+constexpr uint32_t kPeerStageTarget = 32768;  // bytes of one stage over all ranks
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
 }
 
-// The gradient slices of this rank's shard are read straight from every
-// rank's gradient buffer over NVLink (own slice locally), summed in rank order
-// 0..N-1, unscaled and reduced to chunk partials exactly like a single
-// replica.  The last block pushes this rank's partials and non-finite flag
-// into every rank's gathered area and raises their partials flag.
-template <typename GT, bool kMul, int kBatch, int kRanks>
-__device__ __forceinline__ double p2p_thread_sum(const PeerTable& pt, int world,
-                                                 uint64_t shard_begin, uint64_t base,
-                                                 uint64_t n, float* __restrict__ gsum,
-                                                 const ScaleInfo& sc) {
-  double acc = 0.0;
-  if (base + kChunkElems <= n) {
-    // Whole chunk: kBatch vectors of every rank (kBatch * kRanks 16/32-byte
-    // loads, mostly over NVLink) go out before any is added.
-#pragma unroll 1
-    for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kBatch) {
-      RawVec<GT> raw[kBatch][kRanks];
+// Waits until flag >= epoch (wrap-safe); false on timeout or once another wait
+// of this step has given up.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch,
+                                           const DeviceStepState* st, uint64_t timeout_ns) {
+  if (static_cast<int32_t>(ld_volatile(flag) - epoch) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (static_cast<int32_t>(ld_volatile(flag) - epoch) >= 0) return true;
+    if ((it & 63u) == 0u) {
+      if (ld_volatile(&st->kernel_error) != 0u) return false;
+      if (global_ns() - t0 > timeout_ns) return false;
+    }
+  }
+}
+
+// One chunk of the shard from every rank, streamed through shared memory.
+// src_elem: the chunk's first element in the (global) gradient buffers;
+// local: its first element in the shard (gsum index).
+template <typename GT, bool kMul>
+__device__ __forceinline__ bool peer_chunk_bulk(const PeerTable& pt, int world, uint64_t src_elem,
+                                                uint64_t local, uint32_t rows,
+                                                uint32_t stage_bytes, uint8_t* smem,
+                                                uint64_t* full, float* __restrict__ gsum,
+                                                const ScaleInfo& sc, double& acc) {
+  constexpr uint32_t kRowElems = kTreeThreads * kVec;
+  constexpr uint32_t kRowBytes = kRowElems * sizeof(GT);
+  const uint32_t slice = rows * kRowBytes;  // one rank's part of a stage
+  const uint32_t total = kChunkIters / rows;
+  auto issue = [&](uint32_t j) {
+    const uint32_t s = j % kPeerStages;
+    uint8_t* dst = smem + size_t(s) * stage_bytes;
+    const uint64_t e0 = src_elem + uint64_t(j) * rows * kRowElems;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
+    for (int q = 0; q < world; ++q)
+      bulk_load(dst + size_t(q) * slice, static_cast<const GT*>(pt.grads[q]) + e0, slice,
+                &full[s]);
+  };
+  uint32_t issued = 0;
+  if (threadIdx.x == 0)
+    for (; issued < kPeerStages && issued < total; ++issued) issue(issued);
+  for (uint32_t j = 0; j < total; ++j) {
+    const uint32_t s = j % kPeerStages;
+    const bool ok = mbar_wait(&full[s], (j / kPeerStages) & 1u);
+    if (ok) {
+      const uint8_t* base = smem + size_t(s) * stage_bytes + threadIdx.x * kVec * sizeof(GT);
+      for (uint32_t k = 0; k < rows; ++k) {
+        float sum[kVec];
+        lds_grad8(reinterpret_cast<const GT*>(base + k * kRowBytes), sum);
+        for (int q = 1; q < world; ++q) {
+          float x[kVec];
+          lds_grad8(reinterpret_cast<const GT*>(base + size_t(q) * slice + k * kRowBytes), x);
 #pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const uint64_t e0 = base + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec) +
-                            static_cast<uint64_t>(threadIdx.x) * kVec;
-#pragma unroll
-        for (int q = 0; q < kRanks; ++q)
-          if (q < world) raw[b][q].load(static_cast<const GT*>(pt.grads[q]) + shard_begin + e0);
-      }
-#pragma unroll
-      for (int b = 0; b < kBatch; ++b) {
-        const uint64_t e0 = base + static_cast<uint64_t>(k0 + b) * (kTreeThreads * kVec) +
-                            static_cast<uint64_t>(threadIdx.x) * kVec;
-        float s[kVec];
-        raw[b][0].unpack(s);
-#pragma unroll
-        for (int q = 1; q < kRanks; ++q)
-          if (q < world) {
-            float x[kVec];
-            raw[b][q].unpack(x);
-#pragma unroll
-            for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
-          }
-        __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
-        __stcg(reinterpret_cast<float4*>(gsum + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
-        acc = add_squares8<kMul>(acc, s, sc);
+          for (uint32_t e = 0; e < kVec; ++e) sum[e] = __fadd_rn(sum[e], x[e]);
+        }
+        float* out = gsum + local + uint64_t(j * rows + k) * kRowElems + threadIdx.x * kVec;
+        __stcg(reinterpret_cast<float4*>(out), make_float4(sum[0], sum[1], sum[2], sum[3]));
+        __stcg(reinterpret_cast<float4*>(out + 4), make_float4(sum[4], sum[5], sum[6], sum[7]));
+        acc = add_squares8<kMul>(acc, sum, sc);
       }
     }
-    return acc;
+    // Stage s is fully read (or someone gave up): refill it or leave together.
+    if (__syncthreads_or(ok ? 0 : 1)) {
+      if (threadIdx.x == 0)
+        for (uint32_t i = j; i < issued; ++i)  // copies still in flight
+          mbar_wait(&full[i % kPeerStages], (i / kPeerStages) & 1u);
+      return false;
+    }
+    if (threadIdx.x == 0 && issued < total) issue(issued++);
   }
+  return true;
+}
+
+// The ragged last chunk (fewer than 65,536 valid elements), element-wise from
+// global memory with the same order of additions.
+template <typename GT, bool kMul>
+__device__ __forceinline__ double peer_chunk_ragged(const PeerTable& pt, int world,
+                                                    uint64_t shard_begin, uint64_t base,
+                                                    uint64_t n, float* __restrict__ gsum,
+                                                    const ScaleInfo& sc) {
+  double acc = 0.0;
   for (uint32_t k = 0; k < kChunkIters; ++k) {
     const uint64_t e0 = base + static_cast<uint64_t>(k) * (kTreeThreads * kVec) +
                         static_cast<uint64_t>(threadIdx.x) * kVec;
@@ -1389,101 +1458,288 @@ __device__ __forceinline__ double p2p_thread_sum(const PeerTable& pt, int world,
 #pragma unroll
       for (uint32_t j = 0; j < kVec; ++j) s[j] = __fadd_rn(s[j], x[j]);
     }
-    if (e0 + kVec <= n) {
-      __stcg(reinterpret_cast<float4*>(gsum + e0), make_float4(s[0], s[1], s[2], s[3]));
-      __stcg(reinterpret_cast<float4*>(gsum + e0 + 4), make_float4(s[4], s[5], s[6], s[7]));
-    } else {
-      for (uint32_t j = 0; j < kVec && e0 + j < n; ++j) gsum[e0 + j] = s[j];
-    }
+    for (uint32_t j = 0; j < kVec && e0 + j < n; ++j) gsum[e0 + j] = s[j];
     acc = add_squares8<kMul>(acc, s, sc);
   }
   return acc;
 }
 
-template <typename GT, int kBatch, int kRanks>
+template <typename GT>
 __global__ void __launch_bounds__(kTreeThreads)
-    zero1_p2p_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
-                            uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
-                            FinalizeParams fp, float* __restrict__ gsum,
-                            double* __restrict__ send, uint32_t epoch, DeviceStepState* st) {
+    zero1_peer_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
+                             uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
+                             FinalizeParams fp, float* __restrict__ gsum, uint32_t rows,
+                             uint32_t stage_bytes, uint32_t epoch, DeviceStepState* st,
+                             uint64_t timeout_ns) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ double warp_sums[kTreeThreads / 32];
   __shared__ uint32_t s_last;
-  if (st->kernel_error) return;  // a barrier of this step already gave up
-  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
-  bool bad = false;
-  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
-    const uint64_t base = static_cast<uint64_t>(c) * kChunkElems;
-    const double acc =
-        sc.mul
-            ? p2p_thread_sum<GT, true, kBatch, kRanks>(pt, world, shard_begin, base, n_valid,
-                                                       gsum, sc)
-            : p2p_thread_sum<GT, false, kBatch, kRanks>(pt, world, shard_begin, base, n_valid,
-                                                        gsum, sc);
-    bad |= !isfinite(acc);
-    const double total = block_fold(acc, warp_sums);
-    if (threadIdx.x == 0) send[c] = total;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kPeerStages) * stage_bytes);
+  const uint32_t c = blockIdx.x;
+  // Gradient barrier.  This rank's gradient buffer was written by work that
+  // completed before this kernel started; announce it, then wait for all.
+  bool ok = true;
+  if (threadIdx.x < static_cast<unsigned>(world)) {
+    __threadfence_system();
+    *reinterpret_cast<volatile uint32_t*>(pt.flags[threadIdx.x] + kSlotGrads * kMaxRanks +
+                                          rank) = epoch;
+    ok = wait_epoch(pt.flags[rank] + kSlotGrads * kMaxRanks + threadIdx.x, epoch, st,
+                    timeout_ns);
+    if (!ok) atomicOr(&st->kernel_error, 2u);
   }
-  const int any_bad = __syncthreads_or(bad ? 1 : 0);
   if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kPeerStages; ++s) mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  ok = __syncthreads_or(ok ? 0 : 1) == 0;
+  // The peers' gradients (published before their flags) are read by the bulk
+  // copy engine: order the flag observations before those reads.
+  __threadfence_system();
+  if (threadIdx.x == 0) asm volatile("fence.proxy.async;" ::: "memory");
+  __syncthreads();
+  const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
+  const uint64_t base = uint64_t(c) * kChunkElems;
+  double acc = 0.0;
+  if (ok && base < n_valid) {
+    if (base + kChunkElems <= n_valid) {
+      ok = sc.mul ? peer_chunk_bulk<GT, true>(pt, world, shard_begin + base, base, rows,
+                                              stage_bytes, smem, full, gsum, sc, acc)
+                  : peer_chunk_bulk<GT, false>(pt, world, shard_begin + base, base, rows,
+                                               stage_bytes, smem, full, gsum, sc, acc);
+    } else {
+      acc = sc.mul ? peer_chunk_ragged<GT, true>(pt, world, shard_begin, base, n_valid, gsum, sc)
+                   : peer_chunk_ragged<GT, false>(pt, world, shard_begin, base, n_valid, gsum,
+                                                  sc);
+    }
+  }
+  const int any_bad = __syncthreads_or(isfinite(acc) ? 0 : 1);
+  const double partial = block_fold(acc, warp_sums);
+  if (threadIdx.x == 0) {
+    if (ok) {
+      const uint64_t slot = uint64_t(rank) * (n_chunks + 1) + c;
+      for (int q = 0; q < world; ++q) pt.gathered[q][slot] = partial;
+    } else {
+      atomicOr(&st->kernel_error, 1u);
+    }
     if (any_bad) atomicOr(&st->nonfinite_accum, 1u);
-    __threadfence();
+    if (c == 0) {
+      st->loss_scale_used = sc.s;  // the update unscales with the same value
+      st->result_nonfinite = 0u;   // raised by the update kernel
+    }
+    __threadfence_system();
     s_last = (atomicAdd(&st->blocks_done, 1u) == gridDim.x - 1) ? 1u : 0u;
   }
   __syncthreads();
-  if (s_last == 0u) return;
-  __threadfence();
-  const double flag = st->nonfinite_accum != 0u ? 1.0 : 0.0;
-  const uint64_t slot = static_cast<uint64_t>(rank) * (n_chunks + 1);
-  for (int q = 0; q < world; ++q) {
-    double* dst = pt.gathered[q] + slot;
-    for (uint32_t c = threadIdx.x; c < n_chunks; c += kTreeThreads) dst[c] = __ldcg(send + c);
-    if (threadIdx.x == 0) dst[n_chunks] = flag;
-  }
+  if (s_last == 0u || threadIdx.x != 0) return;
+  // Last block: the non-finite flag, then the partials flag on every rank.  A
+  // rank whose step failed here announces nothing: its partials are
+  // incomplete, and the others' bounded waits report the failure.
   __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < static_cast<unsigned>(world))
-    *reinterpret_cast<volatile uint32_t*>(pt.flags[threadIdx.x] + kSlotPartials * kMaxRanks +
-                                          rank) = epoch;
-  if (threadIdx.x == 0) {
-    st->nonfinite_accum = 0u;
-    st->blocks_done = 0u;
-  }
+  const double flag = ld_volatile(&st->nonfinite_accum) != 0u ? 1.0 : 0.0;
+  const uint64_t slot = uint64_t(rank) * (n_chunks + 1) + n_chunks;
+  for (int q = 0; q < world; ++q) pt.gathered[q][slot] = flag;
+  __threadfence_system();
+  if (ld_volatile(&st->kernel_error) == 0u)
+    for (int q = 0; q < world; ++q)
+      *reinterpret_cast<volatile uint32_t*>(pt.flags[q] + kSlotPartials * kMaxRanks + rank) =
+          epoch;
+  st->nonfinite_accum = 0u;
+  st->blocks_done = 0u;
   __threadfence_system();
 }
 
-// Waits (bounded) until every rank delivered its partials, then reduces them
-// in global chunk order -- the same norm / clip / skip bits on every rank.
-__global__ void __launch_bounds__(kTreeThreads)
-    zero1_p2p_finalize_kernel(PeerTable pt, int rank, int world, uint32_t per_rank,
-                              uint32_t epoch, DeviceScaler* scaler, DeviceStepState* st,
-                              FinalizeParams fp, uint64_t timeout_ns) {
-  __shared__ double warp_sums[kTreeThreads / 32];
-  __shared__ uint32_t s_ok;
-  if (threadIdx.x == 0) s_ok = st->kernel_error == 0u ? 1u : 0u;
+// Fold of one double per consumer thread (256, named barrier 1; the producer
+// warp never takes part); result valid in consumer thread 0.
+__device__ __forceinline__ double consumer_fold(double v, double* warp_sums) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v = __dadd_rn(v, __shfl_down_sync(kFull, v, off));
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (lane == 0) warp_sums[warp] = v;
+  asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumers) : "memory");
+  double r = 0.0;
+  if (threadIdx.x == 0) {
+    double w[kBulkConsumers / 32];
+#pragma unroll
+    for (int i = 0; i < int(kBulkConsumers / 32); ++i) w[i] = warp_sums[i];
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+#pragma unroll
+      for (int i = 0; i < off; ++i) w[i] = __dadd_rn(w[i], w[i + off]);
+    }
+    r = w[0];
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumers) : "memory");
+  return r;
+}
+
+__global__ void __launch_bounds__(kBulkThreads)
+    zero1_peer_update_kernel(const float* __restrict__ gsum, uint64_t n, uint64_t elem_base,
+                             float* __restrict__ master, float* __restrict__ mom,
+                             float* __restrict__ var, uint16_t* __restrict__ w16,
+                             const uint64_t* __restrict__ offsets,
+                             const uint8_t* __restrict__ decay,
+                             const uint32_t* __restrict__ tile_first, AdamwParams p,
+                             DeviceStepState* st, DeviceScaler* scaler, PeerTable pt,
+                             PeerStores ps, int rank, int world, uint32_t per_rank,
+                             uint32_t epoch, FinalizeParams fp, uint64_t timeout_ns) {
+  using Stage = BulkStage<float>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ double warp_sums[kBulkConsumers / 32];
+  __shared__ float s_clip;
+  __shared__ uint32_t s_go;
+  __shared__ uint32_t s_stop;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(kBulkStages) * Stage::kBytes);
+  uint64_t* empty_bar = full_bar + kBulkStages;
+  uint8_t* staging = smem + size_t(kBulkStages) * Stage::kBytes + kBarrierBytes;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kBulkStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kBulkConsumers / 32);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_go = 0u;
+    s_stop = 0u;
+  }
   __syncthreads();
-  if (s_ok && threadIdx.x < static_cast<unsigned>(world)) {
-    const volatile uint32_t* f = pt.flags[rank] + kSlotPartials * kMaxRanks + threadIdx.x;
-    const uint64_t t0 = global_ns();
-    while (static_cast<int32_t>(*f - epoch) < 0) {
-      if (global_ns() - t0 > timeout_ns) {
-        atomicOr(&st->kernel_error, 2u);
-        s_ok = 0u;
-        break;
+  // Written by the reduce kernel, which completed before this one started.
+  const bool prior_ok = st->kernel_error == 0u;
+  const float scale = st->loss_scale_used;
+  const uint64_t n_full = n / kBulkTile;
+  const uint64_t mine = n_full > blockIdx.x ? (n_full - 1u - blockIdx.x) / gridDim.x + 1u : 0u;
+  bool ok = true;
+  bool bad = false;
+  uint32_t i = 0;  // producer: tiles issued
+  if (threadIdx.x >= kBulkConsumers) {
+    // Producer warp: lane 0 starts streaming this block's first tiles while
+    // the consumers finalize (those loads do not depend on the clip); it stops
+    // once the consumers have decided not to update.
+    if (threadIdx.x == kBulkConsumers) {
+      for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
+        const uint32_t s = i % kBulkStages;
+        if (i >= kBulkStages) {
+          if (!mbar_wait(&empty_bar[s], ((i / kBulkStages) - 1u) & 1u)) {
+            ok = false;
+            break;
+          }
+          if (*reinterpret_cast<volatile uint32_t*>(&s_stop)) break;
+        }
+        uint8_t* base = smem + size_t(s) * Stage::kBytes;
+        const uint64_t e0 = tile * kBulkTile;
+        mbar_arrive_expect_tx(&full_bar[s], Stage::kBytes);
+        bulk_load(base, gsum + e0, Stage::kG, &full_bar[s]);
+        bulk_load(base + Stage::kG, master + e0, Stage::kF, &full_bar[s]);
+        bulk_load(base + Stage::kG + Stage::kF, mom + e0, Stage::kF, &full_bar[s]);
+        bulk_load(base + Stage::kG + 2 * Stage::kF, var + e0, Stage::kF, &full_bar[s]);
+      }
+    }
+  } else {
+    const uint32_t t = threadIdx.x;
+    // Finalize: wait (bounded) for every rank's partials, reduce them with the
+    // single-replica tree, decide.
+    bool wok = prior_ok;
+    if (wok && t < static_cast<unsigned>(world)) {
+      wok = wait_epoch(pt.flags[rank] + kSlotPartials * kMaxRanks + t, epoch, st, timeout_ns);
+      if (!wok) atomicOr(&st->kernel_error, 2u);
+    }
+    if (consumers_all(wok)) {
+      __threadfence_system();
+      const PartialsView view{pt.gathered[rank], per_rank, per_rank + 1};
+      const double sum =
+          consumer_fold(finalize_lane_sum(view, uint32_t(world) * per_rank, t), warp_sums);
+      if (t == 0) {
+        uint32_t nonfinite = 0u;
+        for (int q = 0; q < world; ++q)
+          nonfinite |= __ldcg(pt.gathered[rank] + uint64_t(q) * (per_rank + 1) + per_rank) != 0.0
+                           ? 1u
+                           : 0u;
+        // Only block 0 reads and writes the scaler; the clip and the skip
+        // decision do not depend on the scaler's step count.
+        const StepDecision d = decide_step(
+            sum, nonfinite, scale, fp.dynamic && blockIdx.x == 0 ? scaler->good_steps : 0u, fp);
+        if (blockIdx.x == 0) {
+          write_decision(d, sum, nonfinite, scale, st, scaler, fp);
+          __threadfence();
+        }
+        s_clip = d.clip_apply;
+        s_go = d.skipped ? 0u : 1u;
+      }
+    }
+    if (t == 0 && s_go == 0u) s_stop = 1u;
+    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumers) : "memory");
+    if (s_go == 0u) {
+      // No update: take back the tiles the producer already started (each
+      // stage's first use), so no copy lands after the block exits.
+      const uint32_t started = mine < kBulkStages ? uint32_t(mine) : kBulkStages;
+      for (uint32_t u = 0; u < started; ++u) {
+        ok &= mbar_wait(&full_bar[u], 0u);
+        __syncwarp();
+        if ((t & 31) == 0) mbar_arrive(&empty_bar[u]);
+      }
+    } else {
+      const ScaleInfo sc = decode_scale(scale);
+      const float clip = s_clip;
+      ok = sc.mul ? bulk_consume<float, true, true>(smem, full_bar, empty_bar, staging, n_full,
+                                                    elem_base, master, mom, var, w16, offsets,
+                                                    decay, tile_first, p, sc, clip, ps, bad)
+                  : bulk_consume<float, false, true>(smem, full_bar, empty_bar, staging, n_full,
+                                                     elem_base, master, mom, var, w16, offsets,
+                                                     decay, tile_first, p, sc, clip, ps, bad);
+      if (t == 0) {
+        bulk_wait_all();  // the weight stores are complete before the barrier
+        asm volatile("fence.proxy.async;" ::: "memory");
+      }
+      if (blockIdx.x == 0) {  // ragged tail after the last whole tile
+        for (uint64_t e = n_full * kBulkTile + t; e < n; e += kBulkConsumers) {
+          uint32_t k = __ldg(tile_first + e / kTileElems);
+          const float wd = decay_of(elem_base + e, k, offsets, decay, p);
+          const float gv = __fmul_rn(
+              sc.mul ? unscale<true>(gsum[e], sc) : unscale<false>(gsum[e], sc), clip);
+          float m = mom[e], v = var[e];
+          const float t1 = adamw_elem(master[e], gv, m, v, wd, p, bad);
+          master[e] = t1;
+          mom[e] = m;
+          var[e] = v;
+          const uint16_t b = bf16_rne_bits(t1);
+          w16[e] = b;
+#pragma unroll
+          for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
+            if (q < ps.count) ps.w16[q][e] = b;
+        }
       }
     }
   }
-  __syncthreads();
-  if (!s_ok) return;
+  __threadfence_system();  // this thread's peer stores before the block counts as done
+  if (__syncthreads_or(ok ? 0 : 1) && threadIdx.x == kBulkConsumers)
+    for (uint32_t u = i > kBulkStages ? i - kBulkStages : 0u; u < i; ++u)
+      mbar_wait(&full_bar[u % kBulkStages], (u / kBulkStages) & 1u);
+  if (threadIdx.x != 0) {
+    if (bad) atomicOr(&st->result_nonfinite, 1u);
+    return;
+  }
+  if (!ok) atomicOr(&st->kernel_error, 1u);
+  if (bad) atomicOr(&st->result_nonfinite, 1u);
+  // Weight barrier: the last block to finish announces this rank's weights
+  // (every block's stores completed and were fenced before it counted) and
+  // waits for every rank's.  Without an update nothing was stored, and after a
+  // failure it only announces.
   __threadfence_system();
-  const double* gathered = pt.gathered[rank];
-  uint32_t nonfinite = 0u;
-  if (threadIdx.x == 0)
+  if (atomicAdd(&st->blocks_done, 1u) != gridDim.x - 1) return;
+  __threadfence_system();
+  const bool failed = ld_volatile(&st->kernel_error) != 0u;
+  if (s_go) {
     for (int q = 0; q < world; ++q)
-      nonfinite |= __ldcg(gathered + static_cast<uint64_t>(q) * (per_rank + 1) + per_rank) != 0.0
-                       ? 1u
-                       : 0u;
-  finalize_block(PartialsView{gathered, per_rank, per_rank + 1}, nonfinite, st, scaler, fp,
-                 warp_sums);
+      *reinterpret_cast<volatile uint32_t*>(pt.flags[q] + kSlotWeights * kMaxRanks + rank) =
+          epoch;
+    if (!failed)
+      for (int q = 0; q < world; ++q)
+        if (!wait_epoch(pt.flags[rank] + kSlotWeights * kMaxRanks + q, epoch, st, timeout_ns)) {
+          atomicOr(&st->kernel_error, 2u);
+          break;
+        }
+  }
+  st->blocks_done = 0u;
+  __threadfence_system();
 }
 
 int sm_count(int device) {
@@ -1538,7 +1794,6 @@ int update_blocks_per_sm() {
   cudaError_t e;
   if constexpr (kUpdateBulk) {
     allow_bulk_smem<GT, false>();
-    allow_bulk_smem<GT, true>();
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
         &per_sm, adamw_update_bulk_kernel<GT, false>, kBulkThreads,
         bulk_smem_bytes<GT, false>());
@@ -1610,28 +1865,16 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 float* master, float* moment, float* variance, uint16_t* w16,
                                 const uint64_t* offsets, const uint8_t* decay,
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
-                                DeviceStepState* st, int grid, cudaStream_t stream,
-                                const PeerStores* peers) {
+                                DeviceStepState* st, int grid, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  const PeerStores ps = peers ? *peers : PeerStores{};
-  const bool with_peers = ps.count > 0;
-  if (dtype == 0) {
-    if (with_peers)
-      launch_update_typed<float, true>(grads, n, elem_base, master, moment, variance, w16, offsets,
-                                       decay, tile_first_tensor, p, st, grid, stream, ps);
-    else
-      launch_update_typed<float, false>(grads, n, elem_base, master, moment, variance, w16,
-                                        offsets, decay, tile_first_tensor, p, st, grid, stream, ps);
-  } else {
-    if (with_peers)
-      launch_update_typed<uint16_t, true>(grads, n, elem_base, master, moment, variance, w16,
-                                          offsets, decay, tile_first_tensor, p, st, grid, stream,
-                                          ps);
-    else
-      launch_update_typed<uint16_t, false>(grads, n, elem_base, master, moment, variance, w16,
-                                           offsets, decay, tile_first_tensor, p, st, grid, stream,
-                                           ps);
-  }
+  const PeerStores none{};
+  if (dtype == 0)
+    launch_update_typed<float, false>(grads, n, elem_base, master, moment, variance, w16, offsets,
+                                      decay, tile_first_tensor, p, st, grid, stream, none);
+  else
+    launch_update_typed<uint16_t, false>(grads, n, elem_base, master, moment, variance, w16,
+                                         offsets, decay, tile_first_tensor, p, st, grid, stream,
+                                         none);
   return cudaGetLastError();
 }
 
@@ -1660,42 +1903,79 @@ cudaError_t launch_zero1_finalize(const double* gathered, uint32_t ranks, uint32
   return cudaGetLastError();
 }
 
-cudaError_t launch_peer_barrier(const PeerTable& pt, int rank, int world, uint32_t slot,
-                                uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns,
-                                cudaStream_t stream) {
-  peer_barrier_kernel<<<1, 32, 0, stream>>>(pt, rank, world, slot, epoch, st, timeout_ns);
+namespace {
+// Largest power of two of tree rows per rank such that one stage (every
+// rank's rows) stays within kPeerStageTarget; at least one row.
+uint32_t peer_rows_per_stage(int dtype, int world) {
+  const uint32_t row = kTreeThreads * kVec * (dtype == 0 ? 4u : 2u);
+  const uint32_t fit = kPeerStageTarget / (row * uint32_t(world));
+  uint32_t r = 1;
+  while (r * 2 <= fit && r * 2 <= kChunkIters) r *= 2;
+  return r;
+}
+
+size_t peer_reduce_smem(int dtype, int world) {
+  const uint32_t row = kTreeThreads * kVec * (dtype == 0 ? 4u : 2u);
+  return size_t(kPeerStages) * peer_rows_per_stage(dtype, world) * row * uint32_t(world) +
+         kBarrierBytes;
+}
+}  // namespace
+
+int prepare_peer_kernels(int device, int world) {
+  cudaError_t e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<float>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(peer_reduce_smem(0, world)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<uint16_t>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(peer_reduce_smem(1, world)));
+  const int bytes = int(bulk_smem_bytes<float, true>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(zero1_peer_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             bytes);
+  int per_sm = 0;
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, zero1_peer_update_kernel,
+                                                      kBulkThreads, bytes);
+  if (e != cudaSuccess || per_sm <= 0) return -1;
+  return sm_count(device) * per_sm;
+}
+
+cudaError_t launch_zero1_peer_reduce(int dtype, const PeerTable& pt, int rank, int world,
+                                     uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
+                                     const DeviceScaler* scaler, const FinalizeParams& fp,
+                                     float* gsum, uint32_t epoch, DeviceStepState* st,
+                                     uint64_t timeout_ns, cudaStream_t stream) {
+  if (n_chunks == 0 || world < 1 || world > kMaxRanks) return cudaErrorInvalidValue;
+  const uint32_t rows = peer_rows_per_stage(dtype, world);
+  const size_t smem = peer_reduce_smem(dtype, world);
+  const uint32_t stage = uint32_t((smem - kBarrierBytes) / kPeerStages);
+  if (dtype == 0)
+    zero1_peer_reduce_kernel<float><<<n_chunks, kTreeThreads, smem, stream>>>(
+        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, rows, stage, epoch, st,
+        timeout_ns);
+  else
+    zero1_peer_reduce_kernel<uint16_t><<<n_chunks, kTreeThreads, smem, stream>>>(
+        pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, rows, stage, epoch, st,
+        timeout_ns);
   return cudaGetLastError();
 }
 
-cudaError_t launch_zero1_p2p_reduce(int dtype, const PeerTable& pt, int rank, int world,
-                                    uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
-                                    const DeviceScaler* scaler, const FinalizeParams& fp,
-                                    float* gsum, double* send, uint32_t epoch,
-                                    DeviceStepState* st, cudaStream_t stream) {
-  if (n_chunks == 0) return cudaErrorInvalidValue;
-  // Loads in flight per thread: kBatch vectors x up to kRanks ranks (8 per batch).
-#define SLM_P2P_LAUNCH(GT, B, R)                                                          \
-  zero1_p2p_reduce_kernel<GT, B, R><<<n_chunks, kTreeThreads, 0, stream>>>(              \
-      pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, send, epoch, st)
-  if (dtype == 0) {
-    if (world <= 2) SLM_P2P_LAUNCH(float, 4, 2);
-    else if (world <= 4) SLM_P2P_LAUNCH(float, 2, 4);
-    else SLM_P2P_LAUNCH(float, 1, 8);
-  } else {
-    if (world <= 2) SLM_P2P_LAUNCH(uint16_t, 4, 2);
-    else if (world <= 4) SLM_P2P_LAUNCH(uint16_t, 2, 4);
-    else SLM_P2P_LAUNCH(uint16_t, 1, 8);
-  }
-#undef SLM_P2P_LAUNCH
-  return cudaGetLastError();
-}
-
-cudaError_t launch_zero1_p2p_finalize(const PeerTable& pt, int rank, int world,
-                                      uint32_t per_rank, uint32_t epoch, DeviceScaler* scaler,
-                                      DeviceStepState* st, const FinalizeParams& fp,
-                                      uint64_t timeout_ns, cudaStream_t stream) {
-  zero1_p2p_finalize_kernel<<<1, kTreeThreads, 0, stream>>>(pt, rank, world, per_rank, epoch,
-                                                            scaler, st, fp, timeout_ns);
+cudaError_t launch_zero1_peer_update(const float* gsum, uint64_t n, uint64_t elem_base,
+                                     float* master, float* moment, float* variance, uint16_t* w16,
+                                     const uint64_t* offsets, const uint8_t* decay,
+                                     const uint32_t* tile_first_tensor, const AdamwParams& p,
+                                     DeviceStepState* st, DeviceScaler* scaler,
+                                     const PeerTable& pt, const PeerStores& ps, int rank,
+                                     int world, uint32_t per_rank, uint32_t epoch,
+                                     const FinalizeParams& fp, uint64_t timeout_ns, int grid,
+                                     cudaStream_t stream) {
+  const uint64_t tiles = n / kBulkTile;
+  const unsigned blocks =
+      static_cast<unsigned>(tiles == 0 ? 1 : (uint64_t(grid) < tiles ? uint64_t(grid) : tiles));
+  zero1_peer_update_kernel<<<blocks, kBulkThreads, bulk_smem_bytes<float, true>(), stream>>>(
+      gsum, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first_tensor, p, st,
+      scaler, pt, ps, rank, world, per_rank, epoch, fp, timeout_ns);
   return cudaGetLastError();
 }
 

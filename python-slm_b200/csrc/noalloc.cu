@@ -15,6 +15,9 @@
 // contents, so each call first clears the counters that must start at zero;
 // two calls whose work overlaps on the GPU (e.g. on two streams) race on it.
 // Every GPU that loads the library holds the array (about 33 KB) until exit.
+// Its device address is looked up once per device and cached; a
+// cudaDeviceReset drops the module with the array, so a process that resets a
+// device must not call this entry point on that device afterwards.
 #include "handle.h"
 
 #include <mutex>
@@ -137,6 +140,12 @@ extern "C" int slm_grad_norm_noalloc(const void* grads, int dtype, uint64_t n, f
   if (!grads || !out_device) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
   if (dtype != SLM_DTYPE_F32 && dtype != SLM_DTYPE_BF16)
     return fail(SLM_ERR_INVALID_ARGUMENT, "unknown gradient dtype");
+  // A misaligned access would fault the caller's context; refuse it here.
+  const uintptr_t esize = dtype == SLM_DTYPE_F32 ? 4u : 2u;
+  if (reinterpret_cast<uintptr_t>(grads) % esize != 0)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "gradients must be aligned to their element size");
+  if (reinterpret_cast<uintptr_t>(out_device) % alignof(slm_norm_result) != 0)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "out_device must be 8-byte aligned");
   if (n == 0) return fail(SLM_ERR_INVALID_ARGUMENT, "no gradient elements");
   if (n > kMaxElements)
     return fail(SLM_ERR_SIZE_LIMIT,

@@ -153,21 +153,30 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 float* master, float* moment, float* variance, uint16_t* w16,
                                 const uint64_t* offsets, const uint8_t* decay,
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
-                                DeviceStepState* st, int grid, cudaStream_t stream,
-                                const PeerStores* peers = nullptr);
-// ZeRO-1 over peer memory (see zero1.cu).
-cudaError_t launch_peer_barrier(const PeerTable& pt, int rank, int world, uint32_t slot,
-                                uint32_t epoch, DeviceStepState* st, uint64_t timeout_ns,
-                                cudaStream_t stream);
-cudaError_t launch_zero1_p2p_reduce(int dtype, const PeerTable& pt, int rank, int world,
-                                    uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
-                                    const DeviceScaler* scaler, const FinalizeParams& fp,
-                                    float* gsum, double* send, uint32_t epoch,
-                                    DeviceStepState* st, cudaStream_t stream);
-cudaError_t launch_zero1_p2p_finalize(const PeerTable& pt, int rank, int world,
-                                      uint32_t per_rank, uint32_t epoch, DeviceScaler* scaler,
-                                      DeviceStepState* st, const FinalizeParams& fp,
-                                      uint64_t timeout_ns, cudaStream_t stream);
+                                DeviceStepState* st, int grid, cudaStream_t stream);
+// ZeRO-1 over peer memory (see zero1.cu): two kernels per step.
+// The reduce: gradient barrier, rank-ordered sum of this shard's slices of
+// every rank's gradient buffer (bulk copies over NVLink), unscale, chunk
+// partials into every rank's gathered area, then the partials flag.
+cudaError_t launch_zero1_peer_reduce(int dtype, const PeerTable& pt, int rank, int world,
+                                     uint64_t shard_begin, uint64_t n_valid, uint32_t n_chunks,
+                                     const DeviceScaler* scaler, const FinalizeParams& fp,
+                                     float* gsum, uint32_t epoch, DeviceStepState* st,
+                                     uint64_t timeout_ns, cudaStream_t stream);
+// The update: finalize of all ranks' partials in every block, AdamW on the
+// shard with the bf16 tiles stored to every rank, then the weight barrier.
+cudaError_t launch_zero1_peer_update(const float* gsum, uint64_t n, uint64_t elem_base,
+                                     float* master, float* moment, float* variance, uint16_t* w16,
+                                     const uint64_t* offsets, const uint8_t* decay,
+                                     const uint32_t* tile_first_tensor, const AdamwParams& p,
+                                     DeviceStepState* st, DeviceScaler* scaler,
+                                     const PeerTable& pt, const PeerStores& ps, int rank,
+                                     int world, uint32_t per_rank, uint32_t epoch,
+                                     const FinalizeParams& fp, uint64_t timeout_ns, int grid,
+                                     cudaStream_t stream);
+// Sets the peer kernels' shared-memory limits on the current device; returns
+// the update kernel's persistent grid (-1 on failure).
+int prepare_peer_kernels(int device, int world);
 // ZeRO-1: rank-ordered sum of the received gradient slices + unscale + chunk
 // partials (send[n_chunks] receives the non-finite flag), then the finalize of
 // the all-gathered partials.

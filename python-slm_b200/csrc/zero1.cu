@@ -1,4 +1,5 @@
-// ZeRO-1 data-parallel optimizer step over NCCL (NVLink 5 / NVSwitch).
+// ZeRO-1 data-parallel optimizer step over NVLink 5 / NVSwitch: peer memory
+// (default) or NCCL.
 //
 // Partition: the flat PARAM-001 buffer is cut into 65,536-element chunks; the
 // chunk count is padded to a multiple of the world size and rank r owns
@@ -6,7 +7,19 @@
 // (clipped to P).  Shards are chunk-aligned, so every norm partial is formed
 // from exactly the same elements, in the same order, as on a single replica.
 //
-// One step, all on the caller's stream:
+// Peer-memory step (every rank maps every other rank's gradient buffer,
+// partials area, flags and bf16 weights with CUDA IPC), two kernels on the
+// caller's stream:
+//   1. zero1_peer_reduce_kernel: gradient barrier, then this shard's slices of
+//      every rank's gradient buffer pulled with bulk copies (NVLink for the
+//      peers), f32 sum in rank order 0..N-1, unscale, chunk partials pushed to
+//      every rank, partials flag;
+//   2. zero1_peer_update_kernel: every block waits for all ranks' partials and
+//      reduces them with the single-replica tree (same decision everywhere),
+//      AdamW on the shard with each bf16 tile bulk-stored to every rank, and
+//      the last block's weight barrier.
+//
+// NCCL step, all on the caller's stream:
 //   1. all-to-all of gradient slices (grouped ncclSend/ncclRecv): rank r
 //      receives slice r of every rank's gradient;
 //   2. zero1_reduce_kernel: f32 sum in rank order 0..N-1, unscale, chunk
@@ -94,10 +107,11 @@ uint64_t peer_wait_ms(const slm_opt_handle* h) {
 
 int zero1_wait(slm_opt_handle* h, cudaStream_t s) {
   const auto t0 = Clock::now();
-  // Over peer memory every device wait of a step is bounded (two barriers and
-  // the finalize, each by barrier_timeout_ns), so the host allows for all of
-  // them: a missing rank is then reported by the device and the stream has
-  // drained when this returns.
+  // Over peer memory every device wait of a step is bounded (the gradient
+  // barrier, the wait for every rank's partials and the weight barrier, each
+  // by barrier_timeout_ns), so the host allows for all of them: a missing rank
+  // is then reported by the device and the stream has drained when this
+  // returns.
   const uint64_t limit_ms =
       h->exchange == SLM_ZERO1_PEER ? uint64_t(h->timeout_ms) + 3ull * peer_wait_ms(h)
                                     : uint64_t(h->timeout_ms);
@@ -239,6 +253,14 @@ int setup_peer_exchange(slm_opt_handle* h, cudaStream_t s) {
       }
     }
   }
+  if (!st && ok) {
+    // The peer kernels' shared-memory limits; a failure here also selects NCCL.
+    h->grid_peer_update = prepare_peer_kernels(h->device, N);
+    if (h->grid_peer_update <= 0) {
+      cudaGetLastError();
+      ok = 0;
+    }
+  }
   if (!st) {
     const int32_t v = ok;
     st = h->cuda(cudaMemcpy(d_ok, &v, sizeof(v), cudaMemcpyHostToDevice), "stage agreement");
@@ -276,45 +298,32 @@ namespace {
 
 uint64_t barrier_timeout_ns(const slm_opt_handle* h) { return peer_wait_ms(h) * 1000000ull; }
 
-// One ZeRO-1 step over peer memory, all on stream s (see slm_opt_zero1_set_exchange).
-int peer_step(slm_opt_handle* h, const void* dev, int dtype, const slm_step_config* cfg,
-              cudaStream_t s) {
+// One ZeRO-1 step over peer memory, all on stream s: two kernels, the reduce
+// (gradient barrier in its prologue) and the update (finalize in its prologue,
+// weight barrier in its epilogue).  See slm_opt_zero1_set_exchange.
+int peer_step(slm_opt_handle* h, int dtype, const slm_step_config* cfg, cudaStream_t s) {
   const uint32_t epoch = ++h->epoch;
   const uint64_t tmo = barrier_timeout_ns(h);
   const FinalizeParams fp = finalize_params(h, cfg);
   int st;
-  (void)dev;
   if ((st = phase_begin(h, s))) return st;
-  if ((st = h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotGrads, epoch,
-                                        h->d_state, tmo, s),
-                    "gradient barrier")))
-    return st;
-  if ((st = phase_mark(h, s))) return st;
-  if ((st = h->cuda(launch_zero1_p2p_reduce(dtype, h->peers, h->rank, h->world, h->shard_begin,
-                                            h->shard_len, h->chunks_per_rank, h->d_scaler, fp,
-                                            h->d_gsum, h->d_send, epoch, h->d_state, s),
+  if ((st = h->cuda(launch_zero1_peer_reduce(dtype, h->peers, h->rank, h->world, h->shard_begin,
+                                             h->shard_len, h->chunks_per_rank, h->d_scaler, fp,
+                                             h->d_gsum, epoch, h->d_state, tmo, s),
                     "peer reduce kernel")))
-    return st;
-  if ((st = phase_mark(h, s))) return st;
-  if ((st = h->cuda(launch_zero1_p2p_finalize(h->peers, h->rank, h->world, h->chunks_per_rank,
-                                              epoch, h->d_scaler, h->d_state, fp, tmo, s),
-                    "peer finalize kernel")))
     return st;
   if ((st = phase_mark(h, s))) return st;
   PeerStores ps{};
   for (int q = 0; q < h->world; ++q)
     if (q != h->rank) ps.w16[ps.count++] = h->peers.w16[q] + h->shard_begin;
   const AdamwParams p = adamw_params(cfg);
-  if ((st = h->cuda(launch_adamw_update(SLM_DTYPE_F32, h->d_gsum, h->shard_len, h->shard_begin,
-                                        h->master, h->m1, h->m2, h->w16 + h->shard_begin,
-                                        h->d_offsets, h->d_decay, h->d_tile_first, p, h->d_state,
-                                        h->grid_update[0], s, &ps),
-                    "update kernel")))
-    return st;
-  if ((st = phase_mark(h, s))) return st;
-  if ((st = h->cuda(launch_peer_barrier(h->peers, h->rank, h->world, kSlotWeights, epoch,
-                                        h->d_state, tmo, s),
-                    "weights barrier")))
+  if ((st = h->cuda(launch_zero1_peer_update(h->d_gsum, h->shard_len, h->shard_begin, h->master,
+                                             h->m1, h->m2, h->w16 + h->shard_begin, h->d_offsets,
+                                             h->d_decay, h->d_tile_first, p, h->d_state,
+                                             h->d_scaler, h->peers, ps, h->rank, h->world,
+                                             h->chunks_per_rank, epoch, fp, tmo,
+                                             h->grid_peer_update, s),
+                    "peer update kernel")))
     return st;
   return phase_mark(h, s);
 }
@@ -342,7 +351,7 @@ int zero1_step(slm_opt_handle* h, const void* grads, int dtype, int memory,
                         "gradient to registered buffer")))
         return st;
     }
-    return peer_step(h, h->d_gradbuf, dtype, cfg, s);
+    return peer_step(h, dtype, cfg, s);
   }
   // Stage host gradients on the device first.
   const void* dev = grads;

@@ -139,6 +139,66 @@ class _stdout_to_stderr:
 
 
 
+def _zero1_parity(opt, table, state, grads, dev, opts, rank, world, args) -> dict:
+    """Post-run check of the ZeRO-1 step (collective: every rank runs it).
+
+    From the seeded state, one step on every rank's seeded gradient must give
+    the state hash, norm, clip and loss scale the oracle computed for a single
+    replica stepping on the rank-ordered f32 sum of all ranks' gradients
+    (tests/golden/step_golden.json, key zero1/<N>); then one step in which the
+    last rank's gradient carries an injected +inf must be skipped by every
+    rank (key skip/<N>).  The outcome is AND-ed over the ranks."""
+    import json as _json
+    from pathlib import Path
+
+    import torch
+    import torch.distributed as dist
+
+    from . import synth
+
+    golden_path = Path(__file__).resolve().parents[2] / "tests" / "golden" / "step_golden.json"
+    try:
+        g = _json.loads(golden_path.read_text())
+    except Exception:
+        g = None
+    P = table.parameter_count
+    if g is None or g.get("params") != P or str(world) not in g.get("zero1", {}):
+        return {"checked": False, "reason": f"no golden record for {world} ranks at P={P}"}
+
+    def compare(res, sha, want):
+        import struct
+
+        bits = struct.unpack("<I", struct.pack("<f", float(res.clip_scale)))[0]
+        out = {"state_bit_exact": sha == want["sha256"],
+               "sum_squares_equal": float(res.sum_squares).hex() == want["sum_squares_hex"],
+               "clip_equal": bits == want["clip_scale_bits"],
+               "skipped_equal": int(res.skipped) == want["skipped"],
+               "next_loss_scale_equal": float(res.next_loss_scale) == want["next_loss_scale"]}
+        out["ok"] = all(out.values())
+        return out
+
+    def reload():
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"],
+                       validate=False)
+        opt.set_loss_scale(65536.0)
+
+    with _stdout_to_stderr():
+        reload()
+        res = opt.step(dev, opts)
+        step = compare(res, opt.state_sha256(), g["zero1"][str(world)])
+        bad = grads.copy()
+        if rank == world - 1:
+            synth.inject_nonfinite(bad, 5, table.offsets)
+        reload()
+        res = opt.step(bad, opts)  # host gradients, copied into the exchange buffer
+        skip = compare(res, opt.state_sha256(), g["skip"][str(world)])
+    ok = torch.tensor([1 if (step["ok"] and skip["ok"]) else 0], dtype=torch.int32)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return {"checked": True, "against": "tests/golden/step_golden.json",
+            "case": f"zero1/{world} and skip/{world}", "step": step, "skip": skip,
+            "bit_exact": bool(ok.item()), "all_ranks": True}
+
+
 def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> None:
     """ZeRO-1 step on N GPUs: every rank holds its own seeded bf16 gradient
     (seed = rank) x 65,536; value = P / (max over ranks of the step time)."""
@@ -249,6 +309,8 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
     te = torch.tensor([(time.perf_counter() - t0) * 1e3 / E], dtype=torch.float64)
     dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
+    parity = _zero1_parity(opt, table, state, grads, dev, opts, rank, world, args) \
+        if not getattr(args, "no_parity", False) else {"checked": False, "reason": "--no-parity"}
     opt_exchange = opt.exchange
     opt.close()
     dist.barrier()
@@ -272,11 +334,15 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
                     "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 80,
                     "ms_per_step": e2e_ms,
                     "api": "slm_opt_upload_gradients + slm_opt_step_uploaded"},
-            "gpu_launches": (5 if opt_exchange == _lib.ZERO1_PEER else 3) * K,
+            "gpu_launches": (2 if opt_exchange == _lib.ZERO1_PEER else 3) * K,
             "exchange": "peer-memory" if opt_exchange == _lib.ZERO1_PEER else "nccl",
             "phases_ms": phases_ms,
             "clocks": clk,
             "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale},
+            "parity": parity,
         }
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
+    if parity.get("checked") and not parity["bit_exact"]:
+        raise SystemExit(f"rank {rank}: ZeRO-1 parity check against the oracle's golden step "
+                         "FAILED")

@@ -3,9 +3,9 @@
 The reference (dhilipsiva/python-slm) is Rust and cannot be built here, so its
 golden vectors are read out of its test sources as text and written to
 reference_kats.json next to this script.  Each value records the file:line it
-came from.  Run once where the reference tree is mounted:
+came from.  Run once where the reference tree is mounted, giving its root:
 
-    python tests/golden/make_kats.py /root/reference
+    python tests/golden/make_kats.py <path to the python-slm checkout>
 
 The tests only read the committed JSON; nothing at test time touches the
 reference tree.
@@ -135,4 +135,6 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_kats.py <path to the python-slm checkout>")
+    main(Path(sys.argv[1]))

@@ -172,7 +172,7 @@ def test_zero1_equals_single_replica(table_name, exchange):
         assert p["w32_ok"]
         times, steps = p["phases"]
         assert steps == 3
-        assert len(times) == (5 if exchange == "peer" else 6)
+        assert len(times) == (2 if exchange == "peer" else 6)
         assert all(ms >= 0.0 for ms in times.values()) and sum(times.values()) > 0.0
 
 

@@ -144,3 +144,20 @@ def test_every_handle_entry_point_rejects_null_arguments():
         assert lib.slm_last_error_message().decode() != "no error", name
     assert lib.slm_opt_destroy(None) == _lib.SLM_OK  # like free(NULL)
     assert lib.slm_opt_phase_name(None, 0) is None
+
+
+def test_noalloc_norm_rejects_misaligned_pointers_before_touching_a_device():
+    # A misaligned gradient or result pointer would fault the caller's context
+    # inside the kernel; the entry point refuses it first (no GPU needed).
+    lib = _lib.load()
+    one = ctypes.c_float(1.0)
+    aligned = 0x10000
+    cases = [
+        (aligned + 2, _lib.DTYPE_F32, aligned),   # f32 gradients 2 bytes off
+        (aligned + 1, _lib.DTYPE_BF16, aligned),  # bf16 gradients 1 byte off
+        (aligned, _lib.DTYPE_F32, aligned + 4),   # result not 8-byte aligned
+    ]
+    for grads, dtype, out in cases:
+        st = lib.slm_grad_norm_noalloc(grads, dtype, 16, one, one, out, None)
+        assert st == _lib.SLM_ERR_INVALID_ARGUMENT, (grads, dtype, out)
+        assert "align" in lib.slm_last_error_message().decode()

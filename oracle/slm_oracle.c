@@ -80,6 +80,21 @@ int slmo_gradient_clip_scale(const float* gradients, uint64_t n, float* out_scal
     return SLMO_OK;
 }
 
+/* The sum inside gradient_clip_scale (src/model/oracle.rs:487-496) on its
+ * own: fl(sum + fl(g * g)) in element order.  Returns
+ * SLMO_MODEL_GRADIENT_NONFINITE at a non-finite element (as the reference
+ * does); the sum itself may overflow to inf. */
+int slmo_reference_sum_squares(const float* gradients, uint64_t n, float* out_sum) {
+    float sum = 0.0f;
+    for (uint64_t i = 0; i < n; ++i) {
+        float g = gradients[i];
+        if (!is_finite_f32(g)) return SLMO_MODEL_GRADIENT_NONFINITE;
+        sum = sum + g * g;
+    }
+    *out_sum = sum;
+    return SLMO_OK;
+}
+
 /* Constants of OPT-001, src/model/oracle.rs:469-484 optimizer_rules. */
 #define RULE_BETA1 0.9f
 #define RULE_BETA2 0.95f

@@ -63,6 +63,8 @@ uint16_t slmo_f32_to_bf16_bits(float value);
 float slmo_bf16_bits_to_f32(uint16_t bits);
 float slmo_powi(float base, int32_t exponent);
 int slmo_gradient_clip_scale(const float* gradients, uint64_t n, float* out_scale);
+/* The sequential f32 sum of squares of gradient_clip_scale alone (oracle.rs:487-496). */
+int slmo_reference_sum_squares(const float* gradients, uint64_t n, float* out_sum);
 int slmo_adamw_scalar_step(float theta, float gradient, float moment, float variance,
                            float learning_rate, uint32_t one_based_update, float weight_decay,
                            float* out_master, float* out_moment, float* out_variance,

@@ -101,6 +101,7 @@ def lib() -> ctypes.CDLL:
         "slmo_bf16_bits_to_f32": (F, [ctypes.c_uint16]),
         "slmo_powi": (F, [F, I32]),
         "slmo_gradient_clip_scale": (ctypes.c_int, [P, U64, ctypes.POINTER(F)]),
+        "slmo_reference_sum_squares": (ctypes.c_int, [P, U64, ctypes.POINTER(F)]),
         "slmo_adamw_scalar_step": (ctypes.c_int, [F, F, F, F, F, U32, F, ctypes.POINTER(F),
                                                   ctypes.POINTER(F), ctypes.POINTER(F),
                                                   ctypes.POINTER(ctypes.c_uint16)]),
@@ -146,6 +147,14 @@ def bf16_bits_to_f32(b: int) -> float:
 
 def powi(base: float, exponent: int) -> float:
     return float(lib().slmo_powi(base, exponent))
+
+
+def reference_sum_squares(g: np.ndarray) -> tuple[int, float]:
+    """(status, the reference's sequential f32 sum of squares)."""
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    out = ctypes.c_float()
+    st = lib().slmo_reference_sum_squares(_ptr(g), g.size, ctypes.byref(out))
+    return st, out.value
 
 
 def gradient_clip_scale(g: np.ndarray) -> tuple[int, float]:

@@ -634,6 +634,25 @@ int slm_grad_accumulate(float* acc_device, const void* micro_device, int dtype, 
   return SLM_OK;
 }
 
+int slm_gradient_clip_scale(const float* grads_device, uint64_t n, slm_clip_result* out_device,
+                            void* stream) {
+  if ((!grads_device && n) || !out_device) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (reinterpret_cast<uintptr_t>(grads_device) % 16 != 0)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "gradients must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(out_device) % alignof(slm_clip_result) != 0)
+    return fail(SLM_ERR_INVALID_ARGUMENT, "out_device must be 4-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(&out_device->kernel_error, 0, sizeof(uint32_t), s);
+  if (e == cudaSuccess) {
+    const SeqClipOut out{nullptr, &out_device->sum_squares, &out_device->clip_scale,
+                         &out_device->status};
+    e = launch_sequential_clip(grads_device, n, out, &out_device->kernel_error, s);
+  }
+  if (e != cudaSuccess)
+    return fail(SLM_ERR_CUDA, std::string("clip scale kernel: ") + cudaGetErrorString(e));
+  return SLM_OK;
+}
+
 int slm_opt_norm_pass_accumulate(slm_opt_handle* h, float* acc_device, const void* micro,
                                  int dtype, int memory, int overwrite,
                                  const slm_step_config* cfg, void* stream) {

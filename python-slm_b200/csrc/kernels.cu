@@ -967,7 +967,18 @@ __device__ __forceinline__ bool bulk_consume(uint8_t* smem, uint64_t* full_bar,
   return true;
 }
 
-template <typename GT, bool kPeers>
+// Programmatic dependent launch: the norm pass lets the update grid launch
+// while its own blocks are still running; the update's producer warps start
+// streaming tiles at once (the norm pass writes none of g / master / m / v),
+// and its consumers wait for the norm pass to complete before they read the
+// step's decision.  Without the launch attribute (or after a kernel that does
+// not trigger) the wait returns at once.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename GT>
 __global__ void __launch_bounds__(kBulkThreads)
     adamw_update_bulk_kernel(const GT* __restrict__ g, uint64_t n, uint64_t elem_base,
                              float* __restrict__ master, float* __restrict__ mom,
@@ -975,35 +986,39 @@ __global__ void __launch_bounds__(kBulkThreads)
                              const uint64_t* __restrict__ offsets,
                              const uint8_t* __restrict__ decay,
                              const uint32_t* __restrict__ tile_first, AdamwParams p,
-                             DeviceStepState* st, PeerStores ps) {
+                             DeviceStepState* st) {
   using Stage = BulkStage<GT>;
   extern __shared__ __align__(128) uint8_t smem[];
-  if (st->skipped || st->kernel_error) return;  // uniform for the grid
+  __shared__ float s_scale, s_clip;
+  __shared__ uint32_t s_go, s_stop;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + size_t(kBulkStages) * Stage::kBytes);
   uint64_t* empty_bar = full_bar + kBulkStages;
-  uint8_t* staging = smem + size_t(kBulkStages) * Stage::kBytes + kBarrierBytes;
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kBulkStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kBulkConsumers / 32);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_stop = 0u;
   }
   __syncthreads();
-  const ScaleInfo sc = decode_scale(st->loss_scale_used);
-  const float clip = st->clip_apply;
   const uint64_t n_full = n / kBulkTile;
+  const uint64_t mine = n_full > blockIdx.x ? (n_full - 1u - blockIdx.x) / gridDim.x + 1u : 0u;
   bool ok = true;
   bool bad = false;
   uint32_t i = 0;  // producer: tiles issued
   if (threadIdx.x >= kBulkConsumers) {
-    // Producer warp: lane 0 keeps kBulkStages tiles in flight.
+    // Producer warp: lane 0 keeps kBulkStages tiles in flight; it stops once
+    // the consumers have found that this step does not update.
     if (threadIdx.x == kBulkConsumers) {
       for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
         const uint32_t s = i % kBulkStages;
-        if (i >= kBulkStages && !mbar_wait(&empty_bar[s], ((i / kBulkStages) - 1u) & 1u)) {
-          ok = false;
-          break;
+        if (i >= kBulkStages) {
+          if (!mbar_wait(&empty_bar[s], ((i / kBulkStages) - 1u) & 1u)) {
+            ok = false;
+            break;
+          }
+          if (*reinterpret_cast<volatile uint32_t*>(&s_stop)) break;
         }
         uint8_t* base = smem + size_t(s) * Stage::kBytes;
         const uint64_t e0 = tile * kBulkTile;
@@ -1015,38 +1030,48 @@ __global__ void __launch_bounds__(kBulkThreads)
       }
     }
   } else {
-    ok = sc.mul ? bulk_consume<GT, true, kPeers>(smem, full_bar, empty_bar, staging, n_full,
-                                                 elem_base, master, mom, var, w16, offsets, decay,
-                                                 tile_first, p, sc, clip, ps, bad)
-                : bulk_consume<GT, false, kPeers>(smem, full_bar, empty_bar, staging, n_full,
-                                                  elem_base, master, mom, var, w16, offsets,
-                                                  decay, tile_first, p, sc, clip, ps, bad);
-    if constexpr (kPeers) {
-      if (threadIdx.x == 0) {
-        // The bulk stores finish (and release shared memory) before the
-        // block exits and before the closing barrier publishes them.
-        bulk_wait_all();
-        asm volatile("fence.proxy.async;" ::: "memory");
-      }
+    const uint32_t t = threadIdx.x;
+    pdl_wait();  // the norm pass (decision, loss scale) is complete and visible
+    if (t == 0) {
+      s_go = (st->skipped == 0u && st->kernel_error == 0u) ? 1u : 0u;
+      s_scale = st->loss_scale_used;
+      s_clip = st->clip_apply;
+      if (!s_go) s_stop = 1u;
     }
-    // Ragged tail after the last whole tile: element by element, block 0.
-    if (blockIdx.x == 0) {
-      for (uint64_t i = n_full * kBulkTile + threadIdx.x; i < n; i += kBulkConsumers) {
-        uint32_t k = __ldg(tile_first + i / kTileElems);
-        const float wd = decay_of(elem_base + i, k, offsets, decay, p);
-        const float gv = __fmul_rn(
-            sc.mul ? unscale<true>(ld_grad1(g, i), sc) : unscale<false>(ld_grad1(g, i), sc),
-            clip);
-        float m = mom[i], v = var[i];
-        const float t1 = adamw_elem(master[i], gv, m, v, wd, p, bad);
-        master[i] = t1;
-        mom[i] = m;
-        var[i] = v;
-        w16[i] = bf16_rne_bits(t1);
-        if constexpr (kPeers) {
-#pragma unroll
-          for (uint32_t q = 0; q < uint32_t(kMaxRanks); ++q)
-            if (q < ps.count) ps.w16[q][i] = bf16_rne_bits(t1);
+    asm volatile("bar.sync 1, %0;" ::"n"(kBulkConsumers) : "memory");
+    if (!s_go) {
+      // No update: take back the tiles the producer already started (each
+      // stage's first use), so no copy lands after the block exits.
+      const uint32_t started = mine < kBulkStages ? uint32_t(mine) : kBulkStages;
+      for (uint32_t u = 0; u < started; ++u) {
+        ok &= mbar_wait(&full_bar[u], 0u);
+        __syncwarp();
+        if ((t & 31) == 0) mbar_arrive(&empty_bar[u]);
+      }
+    } else {
+      const ScaleInfo sc = decode_scale(s_scale);
+      const float clip = s_clip;
+      const PeerStores none{};
+      ok = sc.mul ? bulk_consume<GT, true, false>(smem, full_bar, empty_bar, nullptr, n_full,
+                                                  elem_base, master, mom, var, w16, offsets,
+                                                  decay, tile_first, p, sc, clip, none, bad)
+                  : bulk_consume<GT, false, false>(smem, full_bar, empty_bar, nullptr, n_full,
+                                                   elem_base, master, mom, var, w16, offsets,
+                                                   decay, tile_first, p, sc, clip, none, bad);
+      // Ragged tail after the last whole tile: element by element, block 0.
+      if (blockIdx.x == 0) {
+        for (uint64_t e = n_full * kBulkTile + t; e < n; e += kBulkConsumers) {
+          uint32_t k = __ldg(tile_first + e / kTileElems);
+          const float wd = decay_of(elem_base + e, k, offsets, decay, p);
+          const float gv = __fmul_rn(
+              sc.mul ? unscale<true>(ld_grad1(g, e), sc) : unscale<false>(ld_grad1(g, e), sc),
+              clip);
+          float m = mom[e], v = var[e];
+          const float t1 = adamw_elem(master[e], gv, m, v, wd, p, bad);
+          master[e] = t1;
+          mom[e] = m;
+          var[e] = v;
+          w16[e] = bf16_rne_bits(t1);
         }
       }
     }
@@ -1058,7 +1083,6 @@ __global__ void __launch_bounds__(kBulkThreads)
       mbar_wait(&full_bar[u % kBulkStages], (u / kBulkStages) & 1u);
   if (!ok) atomicOr(&st->kernel_error, 1u);
   if (bad) atomicOr(&st->result_nonfinite, 1u);
-  if constexpr (kPeers) __threadfence_system();  // peer stores visible before the closing barrier
 }
 
 // ---- bulk-copy norm pass (SLM_NORM_BULK=1) ------------------------------------
@@ -1160,6 +1184,9 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
   __shared__ double warp_sums[kTreeThreads / 32];
   __shared__ uint32_t s_last;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kNormStages) * kNormStageBytes);
+  // The update pass may launch now: it only prefetches data this kernel does
+  // not write until it has waited for this kernel to complete.
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kNormStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1198,105 +1225,254 @@ __global__ void __launch_bounds__(kTreeThreads, 2)
                  fp, warp_sums);
 }
 
-// ---- the reference's sequential clip check (strict drop-in) ---------------------
-// CanonicalAdamw re-measures the clip of the gradients it is handed with
-// gradient_clip_scale (src/model/oracle.rs:486-507): `sum += g * g` in f32,
-// one element after another, then min(1 / sqrt(sum), 1).  At 135M terms that
-// sequential f32 sum drifts far from the exact one, and the drop-in must take
-// the same accept / reject decision, so it is reproduced exactly: one CTA,
-// lane 0 of warp 1 streams 16 KB tiles into shared memory with cp.async.bulk,
-// thread 0 adds them in order (each add waits for the previous one: about
-// 4 cycles per element, ~0.3 s at 135M).  Elements after the last whole tile
-// are read from global memory.  Waits are bounded as in the other pipelines.
-constexpr uint32_t kRefStages = 4;
-constexpr uint32_t kRefTile = 4096;  // floats per stage (16 KB)
+// ---- the reference's sequential clip scale, exact and parallel ---------------------
+// gradient_clip_scale (src/model/oracle.rs:486-507) adds the squares one after
+// another in f32, s <- fl(s + fl(g*g)), then clip = min(1 / sqrt(s), 1).  At
+// 135M terms that sum drifts far from the exact one (it drops most terms once
+// s is large), and the drop-ins must reproduce it bit for bit.  It is computed
+// here in parallel, exactly:
+//
+//   While s stays in one binade, s = m * 2^E with an integer m < 2^24 and a
+//   fixed ulp 2^E.  Adding q >= 0 then gives fl(s + q) = (m + r) * 2^E with
+//   r = q / 2^E rounded to the nearest integer -- an increment that does not
+//   depend on m, except when q / 2^E lies exactly halfway (ties go to the even
+//   m + r) or when m + r reaches 2^24 (the sum leaves the binade and the ulp
+//   doubles).  So a window of terms is one integer prefix sum of increments;
+//   at the first term that ties or would leave the binade, the prefix before it
+//   is applied, that one term is added with a real f32 add, and the rest of the
+//   window is redone with the new binade.  Only a few dozen terms of 135M ever
+//   take that path (binade changes are logarithmic in the sum's growth).
+//
+// One CTA of 1024 threads walks 8,192-term windows in order (thread t owns
+// terms 8t..8t+7 of a window, so thread order is term order); thread 0 keeps
+// kSeqStages windows in flight with cp.async.bulk.  Increments are reduced
+// with warp shuffles and shared memory; unsigned 32-bit wrap-around can only
+// corrupt prefixes after the first term whose exact prefix already reached
+// 2^24, which is never used.  A non-finite gradient anywhere makes the status
+// MODEL_GRADIENT_NONFINITE (the reference stops at the first one; the outcome
+// is the same); a sum that overflows makes it MODEL_GRADIENT_NORM_NONFINITE.
+// Waits are bounded as in the other pipelines.
+constexpr uint32_t kSeqThreads = 1024;
+constexpr uint32_t kSeqPer = 8;
+constexpr uint32_t kSeqWindow = kSeqThreads * kSeqPer;  // 8,192 terms
+constexpr uint32_t kSeqWindowBytes = kSeqWindow * 4;    // 32 KB
+constexpr uint32_t kSeqStages = 6;
+constexpr uint32_t kNoStop = 0xffffffffu;
 
-__global__ void __launch_bounds__(64, 1)
-    reference_clip_kernel(const float* __restrict__ g, uint64_t n, DeviceStepState* st) {
+// s = m * 2^E: E >= -149, m < 2^24 (for E > -149, m >= 2^23).
+__device__ __forceinline__ void seq_decompose(float s, int32_t& E, uint32_t& m) {
+  const uint32_t b = __float_as_uint(s);
+  const uint32_t exp = (b >> 23) & 0xffu;
+  const uint32_t man = b & 0x7fffffu;
+  E = exp == 0u ? -149 : int32_t(exp) - 150;
+  m = exp == 0u ? man : (man | 0x800000u);
+}
+__device__ __forceinline__ float seq_compose(int32_t E, uint32_t m) {
+  return __uint_as_float((uint32_t(E + 149) << 23) + m);
+}
+// q / 2^E rounded to nearest (exact halves flagged as ties); anything that
+// certainly leaves the binade returns 2^25.
+__device__ __forceinline__ uint32_t seq_increment(float q, int32_t E, bool& tie) {
+  const uint32_t b = __float_as_uint(q);
+  const uint32_t exp = (b >> 23) & 0xffu;
+  const uint32_t man = b & 0x7fffffu;
+  const uint32_t Q = exp == 0u ? man : (man | 0x800000u);
+  const int32_t F = exp == 0u ? -149 : int32_t(exp) - 150;
+  const int32_t d = E - F;
+  tie = false;
+  if (d < 0) return 1u << 25;  // q >= 2^24 ulps of s (or not finite)
+  if (d == 0) return Q;
+  if (d > 25) return 0u;       // q < half an ulp, never a tie
+  const uint32_t half = 1u << (d - 1);
+  const uint32_t rem = Q & ((1u << d) - 1u);
+  tie = rem == half;
+  return (Q >> d) + (rem > half ? 1u : 0u);
+}
+
+__global__ void __launch_bounds__(kSeqThreads, 1)
+    sequential_clip_kernel(const float* __restrict__ g, uint64_t n, SeqClipOut out,
+                           uint32_t* kernel_error) {
   extern __shared__ __align__(128) uint8_t smem[];
-  float* tiles = reinterpret_cast<float*>(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRefStages * kRefTile * sizeof(float));
-  uint64_t* empty = full + kRefStages;
-  if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < kRefStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+  __shared__ uint32_t warp_val[kSeqThreads / 32];
+  __shared__ uint32_t warp_stop[kSeqThreads / 32];
+  __shared__ int32_t s_E;
+  __shared__ uint32_t s_m, s_restart, s_sum_bad, s_stop, s_total;
+  __shared__ float s_sum_bits;
+  const float* ring = reinterpret_cast<const float*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kSeqStages) * kSeqWindowBytes);
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  if (t == 0) {
+    for (uint32_t s = 0; s < kSeqStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_E = -149;
+    s_m = 0u;
+    s_sum_bad = 0u;
   }
   __syncthreads();
-  const uint64_t n_tiles = n / kRefTile;
-  bool ok = true;
+  const uint64_t n_full = n / kSeqWindow;
+  const uint64_t n_windows = n_full + (n % kSeqWindow ? 1u : 0u);
+  auto issue = [&](uint64_t w) {
+    const uint32_t s = uint32_t(w % kSeqStages);
+    mbar_arrive_expect_tx(&full[s], kSeqWindowBytes);
+    bulk_load(smem + size_t(s) * kSeqWindowBytes, g + w * kSeqWindow, kSeqWindowBytes, &full[s]);
+  };
   uint64_t issued = 0;
-  if (threadIdx.x == 32) {
-    for (; issued < n_tiles; ++issued) {
-      const uint32_t s = uint32_t(issued % kRefStages);
-      if (issued >= kRefStages &&
-          !mbar_wait(&empty[s], uint32_t((issued / kRefStages) - 1u) & 1u)) {
-        ok = false;
+  if (t == 0)
+    for (; issued < kSeqStages && issued < n_full; ++issued) issue(issued);
+  bool ok = true, gbad = false;
+  for (uint64_t w = 0; w < n_windows; ++w) {
+    float q[kSeqPer];
+    if (w < n_full) {
+      const uint32_t s = uint32_t(w % kSeqStages);
+      ok = mbar_wait(&full[s], uint32_t(w / kSeqStages) & 1u);
+      if (ok) {
+        const float4 a = *reinterpret_cast<const float4*>(ring + size_t(s) * kSeqWindow + 8 * t);
+        const float4 c =
+            *reinterpret_cast<const float4*>(ring + size_t(s) * kSeqWindow + 8 * t + 4);
+        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
+        q[4] = c.x; q[5] = c.y; q[6] = c.z; q[7] = c.w;
+      }
+    } else {  // the ragged last window: zeros past n add nothing
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        const uint64_t i = w * kSeqWindow + 8 * t + j;
+        q[j] = i < n ? g[i] : 0.0f;
+      }
+    }
+    if (__syncthreads_or(ok ? 0 : 1)) {  // a copy never arrived: leave together
+      ok = false;
+      break;
+    }
+    if (t == 0 && issued < n_full) issue(issued++);  // this window's stage is read
+#pragma unroll
+    for (uint32_t j = 0; j < kSeqPer; ++j) {
+      gbad |= !finite_f32(q[j]);
+      q[j] = __fmul_rn(q[j], q[j]);
+    }
+    uint32_t start = 0;  // first term of the window not yet added
+    for (;;) {           // block-uniform: every value below is read after a barrier
+      if (s_sum_bad) break;
+      const int32_t E = s_E;
+      const uint32_t m = s_m;
+      uint32_t pre[kSeqPer], run = 0, stop = kNoStop;
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        const uint32_t idx = 8 * t + j;
+        bool tie = false;
+        const uint32_t r = idx < start ? 0u : seq_increment(q[j], E, tie);
+        run += r;
+        pre[j] = run;
+        if (tie && stop == kNoStop) stop = idx;
+      }
+      // exclusive prefix of the thread totals over the block
+      uint32_t incl = run;
+#pragma unroll
+      for (uint32_t off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (lane == 31) warp_val[warp] = incl;
+      __syncthreads();
+      if (warp == 0) {
+        uint32_t v = warp_val[lane];
+#pragma unroll
+        for (uint32_t off = 1; off < 32; off <<= 1) {
+          const uint32_t y = __shfl_up_sync(kFull, v, off);
+          if (lane >= off) v += y;
+        }
+        warp_val[lane] = v;
+      }
+      __syncthreads();
+      const uint32_t excl = (incl - run) + (warp ? warp_val[warp - 1] : 0u);
+      const uint32_t total = warp_val[31];
+      // first term whose running sum would leave the binade (exact up to it)
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        const uint32_t idx = 8 * t + j;
+        if (idx >= start && idx < stop && uint64_t(m) + excl + pre[j] >= (1ull << 24)) stop = idx;
+      }
+      const uint32_t wmin = __reduce_min_sync(kFull, stop);
+      if (lane == 0) warp_stop[warp] = wmin;
+      __syncthreads();
+      if (warp == 0) {
+        const uint32_t v = __reduce_min_sync(kFull, warp_stop[lane]);
+        if (lane == 0) {
+          s_stop = v;
+          s_total = total;
+        }
+      }
+      __syncthreads();
+      const uint32_t first = s_stop;
+      if (first == kNoStop) {  // the whole rest of the window stays in the binade
+        if (t == 0) s_m = m + s_total;
+        __syncthreads();
         break;
       }
-      mbar_arrive_expect_tx(&full[s], kRefTile * sizeof(float));
-      bulk_load(tiles + size_t(s) * kRefTile, g + issued * kRefTile, kRefTile * sizeof(float),
-                &full[s]);
-    }
-  } else if (threadIdx.x == 0) {
-    float sum = 0.0f;
-    bool bad = false;
-    for (uint64_t j = 0; j < n_tiles; ++j) {
-      const uint32_t s = uint32_t(j % kRefStages);
-      if (!mbar_wait(&full[s], uint32_t(j / kRefStages) & 1u)) {
-        ok = false;
-        break;
+      if (first >= 8 * t && first < 8 * t + kSeqPer) {  // the owner of the stopping term
+        const uint32_t j0 = first - 8 * t;
+        uint32_t before = excl;
+        float qj = 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < kSeqPer; ++j) {  // no dynamic register indexing
+          if (j + 1 == j0) before += pre[j];
+          if (j == j0) qj = q[j];
+        }
+        const float sum = __fadd_rn(seq_compose(E, m + before), qj);
+        if (!finite_f32(sum)) {
+          s_sum_bad = 1u;
+          s_sum_bits = sum;
+        } else {
+          int32_t E2;
+          uint32_t m2;
+          seq_decompose(sum, E2, m2);
+          s_E = E2;
+          s_m = m2;
+        }
+        s_restart = first + 1;
       }
-      const float4* t = reinterpret_cast<const float4*>(tiles + size_t(s) * kRefTile);
-#pragma unroll 4
-      for (uint32_t k = 0; k < kRefTile / 4; ++k) {
-        const float4 v = t[k];
-        bad |= !(finite_f32(v.x) && finite_f32(v.y) && finite_f32(v.z) && finite_f32(v.w));
-        sum = __fadd_rn(sum, __fmul_rn(v.x, v.x));
-        sum = __fadd_rn(sum, __fmul_rn(v.y, v.y));
-        sum = __fadd_rn(sum, __fmul_rn(v.z, v.z));
-        sum = __fadd_rn(sum, __fmul_rn(v.w, v.w));
-      }
-      mbar_arrive(&empty[s]);
-    }
-    if (ok) {
-      for (uint64_t i = n_tiles * kRefTile; i < n; ++i) {
-        const float x = g[i];
-        bad |= !finite_f32(x);
-        sum = __fadd_rn(sum, __fmul_rn(x, x));
-      }
-      float clip = 1.0f;
-      int32_t status = kStatusOk;
-      if (bad) {
-        status = kStatusGradientNonfinite;
-      } else if (!finite_f32(sum)) {
-        status = kStatusNormNonfinite;
-      } else if (sum != 0.0f) {
-        const float c = __fdiv_rn(1.0f, __fsqrt_rn(sum));
-        clip = c < 1.0f ? c : 1.0f;
-      }
-      st->sum_squares = double(sum);
-      st->grad_norm = double(__fsqrt_rn(sum));
-      st->clip_scale = clip;
-      st->clip_apply = 1.0f;  // the gradients arrive clipped
-      st->loss_scale_used = 1.0f;
-      st->next_loss_scale = 1.0f;
-      st->skipped = status == kStatusOk ? 0u : 1u;
-      st->nonfinite = status == kStatusOk ? 0u : 1u;
-      st->result_nonfinite = 0u;
-      st->rejected = 0u;
-      st->status = status;
+      __syncthreads();
+      start = s_restart;
+      if (start >= kSeqWindow) break;
     }
   }
-  // After an expired wait the producer waits (bounded) for its copies still
-  // in flight before the block exits.
-  if (__syncthreads_or(ok ? 0 : 1)) {
-    if (threadIdx.x == 32)
-      for (uint64_t u = issued > kRefStages ? issued - kRefStages : 0; u < issued; ++u)
-        mbar_wait(&full[u % kRefStages], uint32_t(u / kRefStages) & 1u);
-    if (threadIdx.x == 0) atomicOr(&st->kernel_error, 1u);
+  // After a failed wait thread 0 waits (bounded) for its copies in flight.
+  if (!ok && t == 0)
+    for (uint64_t u = issued > kSeqStages ? issued - kSeqStages : 0; u < issued; ++u)
+      mbar_wait(&full[u % kSeqStages], uint32_t(u / kSeqStages) & 1u);
+  const int any_bad = __syncthreads_or(gbad ? 1 : 0);
+  if (t != 0) return;
+  if (!ok) {
+    atomicOr(kernel_error, 1u);
+    return;
+  }
+  const float sum = s_sum_bad ? s_sum_bits : seq_compose(s_E, s_m);
+  int32_t status = kStatusOk;
+  float clip = 1.0f;
+  if (any_bad) {
+    status = kStatusGradientNonfinite;
+  } else if (!finite_f32(sum)) {
+    status = kStatusNormNonfinite;
+  } else if (sum != 0.0f) {
+    const float c = __fdiv_rn(1.0f, __fsqrt_rn(sum));
+    clip = c < 1.0f ? c : 1.0f;
+  }
+  if (out.st) {
+    DeviceStepState* st = out.st;
+    st->sum_squares = double(sum);
+    st->grad_norm = double(__fsqrt_rn(sum));
+    st->clip_scale = clip;
+    st->clip_apply = 1.0f;  // the gradients arrive clipped
+    st->loss_scale_used = 1.0f;
+    st->next_loss_scale = 1.0f;
+    st->skipped = status == kStatusOk ? 0u : 1u;
+    st->nonfinite = status == kStatusOk ? 0u : 1u;
+    st->result_nonfinite = 0u;
+    st->rejected = 0u;
+    st->status = status;
+  } else {
+    *out.sum = sum;
+    *out.clip = clip;
+    *out.status = status;
   }
 }
 
@@ -1359,8 +1535,18 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
 // this rank's weights and waits, bounded, for every rank's).
 // Every wait is bounded by timeout_ns; after a wait of a step has given up
 // (kernel_error), later waits of the step return at once.
-constexpr uint32_t kPeerStages = 3;
-constexpr uint32_t kPeerStageTarget = 32768;  // bytes of one stage over all ranks
+#ifndef SLM_PEER_LOADS
+#define SLM_PEER_LOADS 0
+#endif
+#ifndef SLM_PEER_STAGES
+#define SLM_PEER_STAGES 3
+#endif
+#ifndef SLM_PEER_STAGE_BYTES
+#define SLM_PEER_STAGE_BYTES 32768
+#endif
+constexpr bool kPeerLoads = SLM_PEER_LOADS != 0;     // plain loads instead of bulk copies
+constexpr uint32_t kPeerStages = SLM_PEER_STAGES;
+constexpr uint32_t kPeerStageTarget = SLM_PEER_STAGE_BYTES;  // one stage over all ranks
 
 __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
@@ -1438,6 +1624,47 @@ __device__ __forceinline__ bool peer_chunk_bulk(const PeerTable& pt, int world, 
   return true;
 }
 
+// The same whole chunk with plain 16/32-byte loads instead of bulk copies:
+// kBatch tree rows of every rank (kBatch * kRanks loads per thread, mostly over
+// NVLink) go out before any is added.
+template <typename GT, bool kMul, int kBatch, int kRanks>
+__device__ __forceinline__ double peer_chunk_loads(const PeerTable& pt, int world,
+                                                   uint64_t src_elem, uint64_t local,
+                                                   float* __restrict__ gsum,
+                                                   const ScaleInfo& sc) {
+  double acc = 0.0;
+#pragma unroll 1
+  for (uint32_t k0 = 0; k0 < kChunkIters; k0 += kBatch) {
+    RawVec<GT> raw[kBatch][kRanks];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const uint64_t e0 = src_elem + uint64_t(k0 + b) * (kTreeThreads * kVec) +
+                          uint64_t(threadIdx.x) * kVec;
+#pragma unroll
+      for (int q = 0; q < kRanks; ++q)
+        if (q < world) raw[b][q].load(static_cast<const GT*>(pt.grads[q]) + e0);
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      float sum[kVec];
+      raw[b][0].unpack(sum);
+#pragma unroll
+      for (int q = 1; q < kRanks; ++q)
+        if (q < world) {
+          float x[kVec];
+          raw[b][q].unpack(x);
+#pragma unroll
+          for (uint32_t e = 0; e < kVec; ++e) sum[e] = __fadd_rn(sum[e], x[e]);
+        }
+      float* out = gsum + local + uint64_t(k0 + b) * (kTreeThreads * kVec) + threadIdx.x * kVec;
+      __stcg(reinterpret_cast<float4*>(out), make_float4(sum[0], sum[1], sum[2], sum[3]));
+      __stcg(reinterpret_cast<float4*>(out + 4), make_float4(sum[4], sum[5], sum[6], sum[7]));
+      acc = add_squares8<kMul>(acc, sum, sc);
+    }
+  }
+  return acc;
+}
+
 // The ragged last chunk (fewer than 65,536 valid elements), element-wise from
 // global memory with the same order of additions.
 template <typename GT, bool kMul>
@@ -1464,7 +1691,9 @@ __device__ __forceinline__ double peer_chunk_ragged(const PeerTable& pt, int wor
   return acc;
 }
 
-template <typename GT>
+// kBatch == 0: bulk copies through shared memory; otherwise plain loads,
+// kBatch rows x kRanks ranks in flight per thread.
+template <typename GT, int kBatch, int kRanks>
 __global__ void __launch_bounds__(kTreeThreads)
     zero1_peer_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
                              uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
@@ -1476,6 +1705,10 @@ __global__ void __launch_bounds__(kTreeThreads)
   __shared__ uint32_t s_last;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kPeerStages) * stage_bytes);
   const uint32_t c = blockIdx.x;
+  // The update kernel may launch once every block of this grid has started:
+  // its producers wait for this grid to complete before they load, and its
+  // consumers wait for the partials flags.
+  pdl_trigger();
   // Gradient barrier.  This rank's gradient buffer was written by work that
   // completed before this kernel started; announce it, then wait for all.
   bool ok = true;
@@ -1487,7 +1720,7 @@ __global__ void __launch_bounds__(kTreeThreads)
                     timeout_ns);
     if (!ok) atomicOr(&st->kernel_error, 2u);
   }
-  if (threadIdx.x == 0) {
+  if (kBatch == 0 && threadIdx.x == 0) {
     for (uint32_t s = 0; s < kPeerStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -1502,10 +1735,17 @@ __global__ void __launch_bounds__(kTreeThreads)
   double acc = 0.0;
   if (ok && base < n_valid) {
     if (base + kChunkElems <= n_valid) {
-      ok = sc.mul ? peer_chunk_bulk<GT, true>(pt, world, shard_begin + base, base, rows,
-                                              stage_bytes, smem, full, gsum, sc, acc)
-                  : peer_chunk_bulk<GT, false>(pt, world, shard_begin + base, base, rows,
-                                               stage_bytes, smem, full, gsum, sc, acc);
+      if constexpr (kBatch == 0) {
+        ok = sc.mul ? peer_chunk_bulk<GT, true>(pt, world, shard_begin + base, base, rows,
+                                                stage_bytes, smem, full, gsum, sc, acc)
+                    : peer_chunk_bulk<GT, false>(pt, world, shard_begin + base, base, rows,
+                                                 stage_bytes, smem, full, gsum, sc, acc);
+      } else {
+        acc = sc.mul ? peer_chunk_loads<GT, true, kBatch, kRanks>(pt, world, shard_begin + base,
+                                                                  base, gsum, sc)
+                     : peer_chunk_loads<GT, false, kBatch, kRanks>(pt, world, shard_begin + base,
+                                                                   base, gsum, sc);
+      }
     } else {
       acc = sc.mul ? peer_chunk_ragged<GT, true>(pt, world, shard_begin, base, n_valid, gsum, sc)
                    : peer_chunk_ragged<GT, false>(pt, world, shard_begin, base, n_valid, gsum,
@@ -1602,19 +1842,31 @@ __global__ void __launch_bounds__(kBulkThreads)
     s_stop = 0u;
   }
   __syncthreads();
-  // Written by the reduce kernel, which completed before this one started.
-  const bool prior_ok = st->kernel_error == 0u;
-  const float scale = st->loss_scale_used;
+  // The reduce kernel's outcome: this kernel may start while the reduce's
+  // last blocks still run (programmatic launch), so it is read after waiting
+  // for the reduce grid; only the producer warp's loads go ahead without it.
+  __shared__ uint32_t s_prior_ok;
+  __shared__ float s_scale;
+  if (threadIdx.x == 0) {
+    pdl_wait();
+    s_prior_ok = st->kernel_error == 0u ? 1u : 0u;
+    s_scale = st->loss_scale_used;
+  }
+  __syncthreads();
+  const bool prior_ok = s_prior_ok != 0u;
+  const float scale = s_scale;
   const uint64_t n_full = n / kBulkTile;
   const uint64_t mine = n_full > blockIdx.x ? (n_full - 1u - blockIdx.x) / gridDim.x + 1u : 0u;
   bool ok = true;
   bool bad = false;
   uint32_t i = 0;  // producer: tiles issued
   if (threadIdx.x >= kBulkConsumers) {
-    // Producer warp: lane 0 starts streaming this block's first tiles while
+    // Producer warp: once the reduce kernel has completed (its sums are this
+    // kernel's input), lane 0 starts streaming this block's first tiles while
     // the consumers finalize (those loads do not depend on the clip); it stops
     // once the consumers have decided not to update.
     if (threadIdx.x == kBulkConsumers) {
+      pdl_wait();
       for (uint64_t tile = blockIdx.x; tile < n_full; tile += gridDim.x, ++i) {
         const uint32_t s = i % kBulkStages;
         if (i >= kBulkStages) {
@@ -1781,11 +2033,10 @@ int norm_partials_grid(int device) {
 }
 
 namespace {
-template <typename GT, bool kPeers>
+template <typename GT>
 void allow_bulk_smem() {
-  cudaFuncSetAttribute(adamw_update_bulk_kernel<GT, kPeers>,
-                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       int(bulk_smem_bytes<GT, kPeers>()));
+  cudaFuncSetAttribute(adamw_update_bulk_kernel<GT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       int(bulk_smem_bytes<GT, false>()));
 }
 
 template <typename GT>
@@ -1793,10 +2044,9 @@ int update_blocks_per_sm() {
   int per_sm = 0;
   cudaError_t e;
   if constexpr (kUpdateBulk) {
-    allow_bulk_smem<GT, false>();
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, adamw_update_bulk_kernel<GT, false>, kBulkThreads,
-        bulk_smem_bytes<GT, false>());
+    allow_bulk_smem<GT>();
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_update_bulk_kernel<GT>,
+                                                      kBulkThreads, bulk_smem_bytes<GT, false>());
   } else {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_update_kernel<GT, false>,
                                                       kUpdateThreads, 0);
@@ -1804,26 +2054,39 @@ int update_blocks_per_sm() {
   return (e != cudaSuccess || per_sm <= 0) ? (kUpdateBulk ? 1 : 2) : per_sm;
 }
 
-template <typename GT, bool kPeers>
-void launch_update_typed(const void* grads, uint64_t n, uint64_t elem_base, float* master,
-                         float* moment, float* variance, uint16_t* w16, const uint64_t* offsets,
-                         const uint8_t* decay, const uint32_t* tile_first, const AdamwParams& p,
-                         DeviceStepState* st, int grid, cudaStream_t stream,
-                         const PeerStores& ps) {
+template <typename GT>
+cudaError_t launch_update_typed(const void* grads, uint64_t n, uint64_t elem_base, float* master,
+                                float* moment, float* variance, uint16_t* w16,
+                                const uint64_t* offsets, const uint8_t* decay,
+                                const uint32_t* tile_first, const AdamwParams& p,
+                                DeviceStepState* st, int grid, cudaStream_t stream) {
   const GT* g = static_cast<const GT*>(grads);
   if constexpr (kUpdateBulk) {
     const uint64_t tiles = n / kBulkTile;
     const unsigned blocks =
         static_cast<unsigned>(tiles == 0 ? 1 : (uint64_t(grid) < tiles ? uint64_t(grid) : tiles));
-    adamw_update_bulk_kernel<GT, kPeers>
-        <<<blocks, kBulkThreads, bulk_smem_bytes<GT, kPeers>(), stream>>>(
-        g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st, ps);
+    // Programmatic stream serialization: may start before the kernel ahead of
+    // it on the stream completes, if that kernel triggers (the norm pass does).
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(kBulkThreads);
+    cfg.dynamicSmemBytes = bulk_smem_bytes<GT, false>();
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, adamw_update_bulk_kernel<GT>, g, n, elem_base, master, moment,
+                              variance, w16, offsets, decay, tile_first, p, st);
   } else {
     const uint64_t tiles = (n + kTileElems - 1) / kTileElems;
     const unsigned blocks =
         static_cast<unsigned>(uint64_t(grid) < tiles ? uint64_t(grid) : tiles);
-    adamw_update_kernel<GT, kPeers><<<blocks, kUpdateThreads, 0, stream>>>(
-        g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st, ps);
+    adamw_update_kernel<GT, false><<<blocks, kUpdateThreads, 0, stream>>>(
+        g, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first, p, st,
+        PeerStores{});
+    return cudaGetLastError();
   }
 }
 }  // namespace
@@ -1867,15 +2130,11 @@ cudaError_t launch_adamw_update(int dtype, const void* grads, uint64_t n, uint64
                                 const uint32_t* tile_first_tensor, const AdamwParams& p,
                                 DeviceStepState* st, int grid, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  const PeerStores none{};
   if (dtype == 0)
-    launch_update_typed<float, false>(grads, n, elem_base, master, moment, variance, w16, offsets,
-                                      decay, tile_first_tensor, p, st, grid, stream, none);
-  else
-    launch_update_typed<uint16_t, false>(grads, n, elem_base, master, moment, variance, w16,
-                                         offsets, decay, tile_first_tensor, p, st, grid, stream,
-                                         none);
-  return cudaGetLastError();
+    return launch_update_typed<float>(grads, n, elem_base, master, moment, variance, w16, offsets,
+                                      decay, tile_first_tensor, p, st, grid, stream);
+  return launch_update_typed<uint16_t>(grads, n, elem_base, master, moment, variance, w16,
+                                       offsets, decay, tile_first_tensor, p, st, grid, stream);
 }
 
 cudaError_t launch_zero1_reduce(int dtype, const void* recv, uint32_t ranks, uint64_t stride,
@@ -1922,11 +2181,11 @@ size_t peer_reduce_smem(int dtype, int world) {
 }  // namespace
 
 int prepare_peer_kernels(int device, int world) {
-  cudaError_t e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<float>,
+  cudaError_t e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<float, 0, 0>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(peer_reduce_smem(0, world)));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<uint16_t>,
+    e = cudaFuncSetAttribute(zero1_peer_reduce_kernel<uint16_t, 0, 0>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(peer_reduce_smem(1, world)));
   const int bytes = int(bulk_smem_bytes<float, true>());
@@ -1947,15 +2206,33 @@ cudaError_t launch_zero1_peer_reduce(int dtype, const PeerTable& pt, int rank, i
                                      float* gsum, uint32_t epoch, DeviceStepState* st,
                                      uint64_t timeout_ns, cudaStream_t stream) {
   if (n_chunks == 0 || world < 1 || world > kMaxRanks) return cudaErrorInvalidValue;
+  if constexpr (kPeerLoads) {
+    // Plain loads: B rows x R ranks in flight per thread (8 loads per batch).
+#define SLM_PEER_LAUNCH(GT, B, R)                                                             \
+  zero1_peer_reduce_kernel<GT, B, R><<<n_chunks, kTreeThreads, 0, stream>>>(                  \
+      pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, 0u, 0u, epoch, st,  \
+      timeout_ns)
+    if (dtype == 0) {
+      if (world <= 2) SLM_PEER_LAUNCH(float, 4, 2);
+      else if (world <= 4) SLM_PEER_LAUNCH(float, 2, 4);
+      else SLM_PEER_LAUNCH(float, 1, 8);
+    } else {
+      if (world <= 2) SLM_PEER_LAUNCH(uint16_t, 4, 2);
+      else if (world <= 4) SLM_PEER_LAUNCH(uint16_t, 2, 4);
+      else SLM_PEER_LAUNCH(uint16_t, 1, 8);
+    }
+#undef SLM_PEER_LAUNCH
+    return cudaGetLastError();
+  }
   const uint32_t rows = peer_rows_per_stage(dtype, world);
   const size_t smem = peer_reduce_smem(dtype, world);
   const uint32_t stage = uint32_t((smem - kBarrierBytes) / kPeerStages);
   if (dtype == 0)
-    zero1_peer_reduce_kernel<float><<<n_chunks, kTreeThreads, smem, stream>>>(
+    zero1_peer_reduce_kernel<float, 0, 0><<<n_chunks, kTreeThreads, smem, stream>>>(
         pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, rows, stage, epoch, st,
         timeout_ns);
   else
-    zero1_peer_reduce_kernel<uint16_t><<<n_chunks, kTreeThreads, smem, stream>>>(
+    zero1_peer_reduce_kernel<uint16_t, 0, 0><<<n_chunks, kTreeThreads, smem, stream>>>(
         pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, rows, stage, epoch, st,
         timeout_ns);
   return cudaGetLastError();
@@ -1973,10 +2250,19 @@ cudaError_t launch_zero1_peer_update(const float* gsum, uint64_t n, uint64_t ele
   const uint64_t tiles = n / kBulkTile;
   const unsigned blocks =
       static_cast<unsigned>(tiles == 0 ? 1 : (uint64_t(grid) < tiles ? uint64_t(grid) : tiles));
-  zero1_peer_update_kernel<<<blocks, kBulkThreads, bulk_smem_bytes<float, true>(), stream>>>(
-      gsum, n, elem_base, master, moment, variance, w16, offsets, decay, tile_first_tensor, p, st,
-      scaler, pt, ps, rank, world, per_rank, epoch, fp, timeout_ns);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kBulkThreads);
+  cfg.dynamicSmemBytes = bulk_smem_bytes<float, true>();
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, zero1_peer_update_kernel, gsum, n, elem_base, master, moment,
+                            variance, w16, offsets, decay, tile_first_tensor, p, st, scaler, pt,
+                            ps, rank, world, per_rank, epoch, fp, timeout_ns);
 }
 
 cudaError_t launch_accumulate(int dtype, float* acc, const void* micro, uint64_t n,
@@ -2021,11 +2307,17 @@ cudaError_t launch_init_from_master(float* master, float* moment, float* varianc
 
 cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
                                   cudaStream_t stream) {
-  const int bytes = int(kRefStages * kRefTile * sizeof(float) + 2 * kRefStages * sizeof(uint64_t));
-  cudaError_t e = cudaFuncSetAttribute(reference_clip_kernel,
+  SeqClipOut out{st, nullptr, nullptr, nullptr};
+  return launch_sequential_clip(g, n, out, &st->kernel_error, stream);
+}
+
+cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
+                                   uint32_t* kernel_error, cudaStream_t stream) {
+  const int bytes = int(kSeqStages * kSeqWindowBytes + kBarrierBytes);
+  cudaError_t e = cudaFuncSetAttribute(sequential_clip_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
-  reference_clip_kernel<<<1, 64, bytes, stream>>>(g, n, st);
+  sequential_clip_kernel<<<1, kSeqThreads, bytes, stream>>>(g, n, out, kernel_error);
   return cudaGetLastError();
 }
 

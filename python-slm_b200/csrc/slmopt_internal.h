@@ -202,6 +202,16 @@ cudaError_t launch_export_f32(const uint16_t* w16, float* dst, uint64_t n, cudaS
 // fills st as the norm pass would for a static scale of 1 without clipping.
 cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
                                   cudaStream_t stream);
+// The same sequential clip scale with its result sent elsewhere: into the step
+// record (st != NULL) or into the three caller-provided device words.
+struct SeqClipOut {
+  DeviceStepState* st;
+  float* sum;
+  float* clip;
+  int32_t* status;
+};
+cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
+                                   uint32_t* kernel_error, cudaStream_t stream);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

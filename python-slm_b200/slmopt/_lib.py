@@ -112,6 +112,17 @@ class NormResult(ctypes.Structure):
     ]
 
 
+class ClipResult(ctypes.Structure):
+    """slm_clip_result (written to device memory by slm_gradient_clip_scale)."""
+
+    _fields_ = [
+        ("sum_squares", ctypes.c_float),
+        ("clip_scale", ctypes.c_float),
+        ("status", ctypes.c_int32),
+        ("kernel_error", ctypes.c_uint32),
+    ]
+
+
 NOALLOC_MAX_ELEMENTS = 268435456
 
 _P = ctypes.c_void_p
@@ -161,6 +172,7 @@ SIGNATURES = [
     ("slm_opt_zero1_exchange", _I, [_P]),
     ("slm_opt_gradient_buffer", _I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_U64)]),
     ("slm_grad_norm_noalloc", _I, [_P, _I, _U64, _F, _F, _P, _P]),
+    ("slm_gradient_clip_scale", _I, [_P, _U64, _P, _P]),
     ("slm_opt_set_loss_scale", _I, [_P, _F, _U32]),
     ("slm_opt_get_loss_scale", _I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_U32)]),
     ("slm_canonical_learning_rate", _I, [_U64, ctypes.POINTER(_F)]),

@@ -629,3 +629,124 @@ def test_accumulated_micro_batches_then_fused_norm_and_update(torch, dtype):
     ores = oracle.step(oracle.make_config(lr=3e-4, t=7, static_scale=65536.0), want_acc,
                        table.offsets, table.decay, ost, threads=THREADS)
     check_equal(res, got, ores, ost)
+
+
+# ---- the trainer's update bookkeeping around the device step (trainer.rs:808-955) ------
+def test_trainer_process_batch_drives_the_device_step(torch):
+    # Two updates of four micro-batches each through B200Trainer: gradients
+    # summed on the device, the last micro-batch fused with the norm pass
+    # (normalised by 65,536 targets), the canonical learning rate, the update
+    # pass and the state hash; the state after each update equals the oracle's
+    # step on the host-summed gradient, and the events carry the reference's
+    # accounting.
+    from slmopt import trainer as tr
+
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    n = table.parameter_count
+    state = synth.optimizer_state(n, 31)
+    ost = {k: v.copy() for k, v in state.items()}
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        run = tr.B200Trainer(opt)
+        cursor = 0
+        for t in (1, 2):
+            micro = [(synth.grads_f32(n, 40 + 4 * t + i) * np.float32(16384.0)).astype(np.float32)
+                     for i in range(4)]
+            events = []
+            for i, m in enumerate(micro):
+                events.append(run.process_batch(cursor, 16_384, 2.0 * (i + 1),
+                                                to_device(torch, m)))
+                cursor += 16_384
+            assert events[:3] == [None, None, None]
+            ev = events[3]
+            acc = micro[0].copy()
+            for m in micro[1:]:
+                acc = (acc + m).astype(np.float32)
+            status, lr = oracle.canonical_learning_rate(t)
+            assert status == 0
+            ores = oracle.step(oracle.make_config(lr=lr, t=t, static_scale=65536.0,
+                                                  nonfinite_policy=1),
+                               acc, table.offsets, table.decay, ost, threads=THREADS)
+            assert ores.status == 0 and not ores.skipped
+            want_sha = oracle.state_sha256(table.names, table.offsets, table.decay, ost)[1]
+            assert ev.one_based_update == t and ev.consumed_targets == 65_536 * t
+            assert ev.valid_targets == 65_536 and not ev.checkpoint_due
+            assert ev.update_state_sha256 == want_sha
+            assert ev.learning_rate_f32_le_hex == tr.f32_le_hex(lr)
+            assert ev.normalized_loss_f64_le_hex == tr.f64_le_hex(20.0 / 65_536.0)
+        # a non-finite micro-batch fails the update and counts nothing
+        clean = (synth.grads_f32(n, 99) * np.float32(16384.0)).astype(np.float32)
+        bad = clean.copy()
+        synth.inject_nonfinite(bad, 2, table.offsets)
+        for _ in range(3):
+            run.process_batch(cursor, 16_384, 1.0, to_device(torch, clean))
+            cursor += 16_384
+        with pytest.raises(tr.TrainerError) as e:
+            run.process_batch(cursor, 16_384, 1.0, to_device(torch, bad))
+        assert e.value.code == "P12_GRADIENT_NONFINITE"
+        assert run.accounting.accumulated_targets == 3 * 16_384
+        assert run.accounting.completed_updates == 2
+
+
+# ---- gradient_clip_scale: the reference's sequential f32 sum (oracle.rs:486-507) -------
+def _clip_cases():
+    rng = np.random.default_rng(5)
+    cases = {
+        "kat_3_4": np.array([3.0, 4.0], np.float32),
+        "zeros": np.zeros(10_000, np.float32),
+        "one": np.array([0.5], np.float32),
+        "empty": np.zeros(0, np.float32),
+    }
+    for n in (7, 8191, 8192, 8193, 65_537, 1_000_003):
+        cases[f"normal_{n}"] = rng.standard_normal(n).astype(np.float32)
+    # exact ties: powers of two whose squares land on half an ulp of the sum
+    cases["powers_of_two"] = (2.0 ** rng.integers(-70, 8, 300_000)).astype(np.float32)
+    cases["subnormal_squares"] = (rng.standard_normal(200_000) * 1e-22).astype(np.float32)
+    cases["leading_zeros"] = np.concatenate(
+        [np.zeros(50_000, np.float32), rng.standard_normal(90_000).astype(np.float32) * 1e-3])
+    cases["drifting"] = (rng.standard_normal(3_000_000) * 1e-3).astype(np.float32)
+    cases["overflow"] = (rng.standard_normal(20_000) * 1e18).astype(np.float32)
+    inf = rng.standard_normal(50_000).astype(np.float32)
+    inf[31_337] = np.inf
+    cases["inf"] = inf
+    nan = rng.standard_normal(50_000).astype(np.float32)
+    nan[9_000] = np.nan
+    cases["nan"] = nan
+    return cases
+
+
+CLIP_CASES = _clip_cases()
+
+
+@pytest.mark.parametrize("name", sorted(CLIP_CASES))
+def test_gradient_clip_scale_is_the_reference_sequential_sum(torch, name):
+    from slmopt.optimizer import gradient_clip_scale
+
+    g = CLIP_CASES[name]
+    dev = torch.from_numpy(g).cuda() if g.size else torch.zeros(0, dtype=torch.float32,
+                                                                 device="cuda")
+    status, got_sum, got_clip = gradient_clip_scale(dev)
+    want_status, want_clip = oracle.gradient_clip_scale(g)
+    sum_status, want_sum = oracle.reference_sum_squares(g)
+    assert status == want_status, (status, want_status)
+    if want_status == 0:
+        assert np.float32(got_sum).view(np.uint32) == np.float32(want_sum).view(np.uint32)
+        assert np.float32(got_clip).view(np.uint32) == np.float32(want_clip).view(np.uint32)
+    elif want_status == oracle.MODEL_GRADIENT_NORM_NONFINITE:
+        assert sum_status == 0 and not np.isfinite(want_sum) and not np.isfinite(got_sum)
+
+
+def test_gradient_clip_scale_at_production_width(torch):
+    # the reference's 135,285,504-element probe shape: a clipped gradient whose
+    # sequential f32 sum drifts ~35 % below the exact one
+    from slmopt.optimizer import gradient_clip_scale
+
+    n = 135_285_504
+    g = synth.grads_f32(n, 1)
+    g *= np.float32(0.9 / float(np.sqrt(np.sum(g.astype(np.float64) ** 2))))
+    status, got_sum, got_clip = gradient_clip_scale(torch.from_numpy(g).cuda())
+    st, want_sum = oracle.reference_sum_squares(g)
+    assert status == 0 and st == 0
+    assert np.float32(got_sum).view(np.uint32) == np.float32(want_sum).view(np.uint32)
+    assert got_clip == 1.0
+    assert got_sum < 0.7 * 0.81  # the drift the exact sum would not show

@@ -138,6 +138,7 @@ def test_every_handle_entry_point_rejects_null_arguments():
         "slm_opt_phase_times": (None, d, 8, ctypes.byref(u32), ctypes.byref(u64)),
         "slm_grad_accumulate": (None, None, 1, 0, 0, None),
         "slm_grad_norm_noalloc": (None, 1, 10, one, one, None, None),
+        "slm_gradient_clip_scale": (None, 10, None, None),
     }
     for name, args in calls.items():
         assert getattr(lib, name)(*args) == _lib.SLM_ERR_INVALID_ARGUMENT, name

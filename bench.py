@@ -424,7 +424,31 @@ def cpu_baseline_sample(table, state, grads, workload: str, seconds: float = 12.
             "sample": f"{len(times)} full {P:,}-param steps ({workload}) with {cores} threads, "
                       f"median {med * 1e3:.1f} ms",
             "ms_per_step": med * 1e3,
-            "single_thread_value": P / single, "single_thread_ms_per_step": single * 1e3}
+            "single_thread_value": P / single, "single_thread_ms_per_step": single * 1e3,
+            "smoke_step": smoke_cpu_step(oracle, cores)}
+
+
+def smoke_cpu_step(oracle, cores: int) -> dict:
+    """The CPU oracle step over the smoke tensor list (4,489,856 params, fp32
+    gradients, clip 1.0, t = 10): single-threaded like the reference's loop,
+    and on every host core; median of 10 each."""
+    from slmopt import GqaDimensions, TensorTable, synth
+
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    P = table.parameter_count
+    state = synth.optimizer_state(P, 0)
+    grads = synth.grads_f32(P, 0)
+    cfg = oracle.make_config(lr=3e-4, t=10)
+    out = {"params": P, "tensors": len(table)}
+    for key, threads in (("single_thread_ms", 1), ("all_cores_ms", cores)):
+        st = {k: v.copy() for k, v in state.items()}
+        times = []
+        for _ in range(11):
+            t0 = time.perf_counter()
+            oracle.step(cfg, grads, table.offsets, table.decay, st, threads=threads)
+            times.append((time.perf_counter() - t0) * 1e3)
+        out[key] = statistics.median(times[1:])
+    return out
 
 
 def run_reference(args) -> None:

@@ -1272,6 +1272,7 @@ __device__ __forceinline__ float seq_compose(int32_t E, uint32_t m) {
 }
 // q / 2^E rounded to nearest (exact halves flagged as ties); anything that
 // certainly leaves the binade returns 2^25.
+// Branch-free: the terms of one warp have different exponents.
 __device__ __forceinline__ uint32_t seq_increment(float q, int32_t E, bool& tie) {
   const uint32_t b = __float_as_uint(q);
   const uint32_t exp = (b >> 23) & 0xffu;
@@ -1279,14 +1280,15 @@ __device__ __forceinline__ uint32_t seq_increment(float q, int32_t E, bool& tie)
   const uint32_t Q = exp == 0u ? man : (man | 0x800000u);
   const int32_t F = exp == 0u ? -149 : int32_t(exp) - 150;
   const int32_t d = E - F;
-  tie = false;
-  if (d < 0) return 1u << 25;  // q >= 2^24 ulps of s (or not finite)
-  if (d == 0) return Q;
-  if (d > 25) return 0u;       // q < half an ulp, never a tie
-  const uint32_t half = 1u << (d - 1);
-  const uint32_t rem = Q & ((1u << d) - 1u);
-  tie = rem == half;
-  return (Q >> d) + (rem > half ? 1u : 0u);
+  // For d in [1, 31] the shift arithmetic below is exact; d > 25 gives 0 and
+  // no tie there (Q < 2^24 <= half).  d == 0 adds Q ulps exactly; d < 0 means
+  // q is at least 2^24 ulps of s (or not finite): it certainly leaves the binade.
+  const uint32_t dc = uint32_t(d < 1 ? 1 : (d > 31 ? 31 : d));
+  const uint32_t half = 1u << (dc - 1u);
+  const uint32_t rem = Q & ((half << 1) - 1u);
+  const uint32_t r = (Q >> dc) + (rem > half ? 1u : 0u);
+  tie = d > 0 && rem == half;
+  return d < 0 ? (1u << 25) : (d == 0 ? Q : r);
 }
 
 __global__ void __launch_bounds__(kSeqThreads, 1)
@@ -1297,6 +1299,7 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
   __shared__ uint32_t warp_stop[kSeqThreads / 32];
   __shared__ int32_t s_E;
   __shared__ uint32_t s_m, s_restart, s_sum_bad, s_stop, s_total;
+  __shared__ uint32_t s_fast_total[2], s_fast_tie[2];
   __shared__ float s_sum_bits;
   const float* ring = reinterpret_cast<const float*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kSeqStages) * kSeqWindowBytes);
@@ -1348,6 +1351,46 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
     for (uint32_t j = 0; j < kSeqPer; ++j) {
       gbad |= !finite_f32(q[j]);
       q[j] = __fmul_rn(q[j], q[j]);
+    }
+    // Fast path: the window's total increment for the current binade and
+    // whether any term ties; if nothing ties and the sum stays in the binade
+    // the whole window is one integer add.  Totals are clamped at 2^24 (any
+    // such total leaves the binade, which is all that is tested).
+    if (!s_sum_bad) {
+      const int32_t E = s_E;
+      const uint32_t m = s_m;
+      uint32_t tsum = 0;
+      bool tie_any = false;
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        bool tie;
+        tsum += seq_increment(q[j], E, tie);  // <= 8 * 2^25: no wrap
+        tie_any |= tie;
+      }
+      const uint32_t wsum = __reduce_add_sync(kFull, tsum < (1u << 24) ? tsum : (1u << 24));
+      const uint32_t wtie = __reduce_or_sync(kFull, tie_any ? 1u : 0u);
+      if (lane == 0) {
+        warp_val[warp] = wsum < (1u << 24) ? wsum : (1u << 24);
+        warp_stop[warp] = wtie;
+      }
+      __syncthreads();
+      // The window's verdict goes to slot w % 2, so the next window's write
+      // never meets a thread still reading this one (no third barrier).
+      const uint32_t slot = uint32_t(w & 1u);
+      if (warp == 0) {
+        const uint32_t v = __reduce_add_sync(kFull, warp_val[lane]);
+        const uint32_t tw = __reduce_or_sync(kFull, warp_stop[lane]);
+        if (lane == 0) {
+          s_fast_total[slot] = v;
+          s_fast_tie[slot] = tw;
+        }
+      }
+      __syncthreads();
+      const uint32_t total = s_fast_total[slot];
+      if (s_fast_tie[slot] == 0u && uint64_t(m) + total < (1ull << 24)) {
+        if (t == 0) s_m = m + total;
+        continue;  // the next window starts with a barrier
+      }
     }
     uint32_t start = 0;  // first term of the window not yet added
     for (;;) {           // block-uniform: every value below is read after a barrier

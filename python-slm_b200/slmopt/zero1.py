@@ -199,6 +199,64 @@ def _zero1_parity(opt, table, state, grads, dev, opts, rank, world, args) -> dic
             "bit_exact": bool(ok.item()), "all_ranks": True}
 
 
+def _zero1_stress(rank: int, world: int) -> dict:
+    """BASELINE's 100-step stress run (collective), checked against the
+    oracle's trajectory for this rank count (tests/golden/stress_golden.json):
+    per update the skip decision, the f64 norm's bits, the clip's bits and the
+    next loss scale, and the final state's SHA-256.  Smoke tensor list, inputs
+    from slmopt.stress; the outcome is AND-ed over the ranks."""
+    import json as _json
+    import struct
+    from pathlib import Path
+
+    import torch
+    import torch.distributed as dist
+
+    from . import stress
+    from .layout import GqaDimensions
+    from .optimizer import StepOptions
+
+    golden_path = Path(__file__).resolve().parents[2] / "tests" / "golden" / "stress_golden.json"
+    try:
+        g = _json.loads(golden_path.read_text())["worlds"][str(world)]
+    except Exception:
+        return {"checked": False, "reason": f"no golden trajectory for {world} ranks"}
+    table = TensorTable.from_dimensions(GqaDimensions.smoke())
+    P = table.parameter_count
+    ids = [unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    from . import synth
+
+    with _stdout_to_stderr():
+        opt = Zero1Adamw(table, rank, world, ids[0], device=torch.cuda.current_device(),
+                         timeout_ms=120000)
+        st = synth.optimizer_state(P, 0)
+        opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"], validate=False)
+        opt.set_loss_scale(65536.0)
+        scale, mismatches = 65536.0, []
+        for t in range(1, stress.STEPS + 1):
+            bits = stress.rank_gradient(P, table.offsets, rank, t, scale)
+            r = opt.step(bits, StepOptions(learning_rate=stress.learning_rate(t),
+                                           one_based_update=t,
+                                           loss_scale_mode=_lib.SCALE_DYNAMIC))
+            got = [int(r.skipped), float(r.sum_squares).hex(),
+                   struct.unpack("<I", struct.pack("<f", float(r.clip_scale)))[0],
+                   float(r.next_loss_scale)]
+            if got != g["trace"][t - 1]:
+                mismatches.append(t)
+            scale = r.next_loss_scale
+        sha = opt.state_sha256()
+        opt.close()
+    ok = not mismatches and sha == g["final_sha256"]
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return {"checked": True, "against": "tests/golden/stress_golden.json", "updates": stress.STEPS,
+            "params": P, "skipped_updates": g["skipped_updates"],
+            "trajectory_equal": not mismatches, "mismatched_updates": mismatches[:10],
+            "final_state_equal": sha == g["final_sha256"], "bit_exact": bool(flag.item()),
+            "all_ranks": True}
+
+
 def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> None:
     """ZeRO-1 step on N GPUs: every rank holds its own seeded bf16 gradient
     (seed = rank) x 65,536; value = P / (max over ranks of the step time)."""
@@ -306,13 +364,18 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
         opt.step_uploaded(slot, opts, stream=stream)
         slot = nxt
     torch.cuda.synchronize()
-    te = torch.tensor([(time.perf_counter() - t0) * 1e3 / E], dtype=torch.float64)
-    dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    mine = (time.perf_counter() - t0) * 1e3 / E
+    per_rank = [torch.zeros(1, dtype=torch.float64) for _ in range(world)]
+    dist.all_gather(per_rank, torch.tensor([mine], dtype=torch.float64))
+    per_rank_ms = [float(x.item()) for x in per_rank]
+    e2e_ms = max(per_rank_ms)
     parity = _zero1_parity(opt, table, state, grads, dev, opts, rank, world, args) \
         if not getattr(args, "no_parity", False) else {"checked": False, "reason": "--no-parity"}
     opt_exchange = opt.exchange
     opt.close()
+    dist.barrier()
+    stress_check = _zero1_stress(rank, world) if not getattr(args, "no_parity", False) \
+        else {"checked": False, "reason": "--no-parity"}
     dist.barrier()
     if rank == 0:
         peak, peak_kind = hbm_peak()
@@ -332,7 +395,8 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
                          "hbm_peak_gbs": peak, "hbm_peak_source": peak_kind},
             "e2e": {"value": P / (e2e_ms * 1e-3), "unit": unit,
                     "h2d_bytes_per_step": int(grads.nbytes), "d2h_bytes_per_step": 80,
-                    "ms_per_step": e2e_ms,
+                    "ms_per_step": e2e_ms, "per_rank_ms": per_rank_ms,
+                    "host_to_device_gbs_all_ranks": world * grads.nbytes / (e2e_ms * 1e-3) / 1e9,
                     "api": "slm_opt_upload_gradients + slm_opt_step_uploaded"},
             "gpu_launches": (2 if opt_exchange == _lib.ZERO1_PEER else 3) * K,
             "exchange": "peer-memory" if opt_exchange == _lib.ZERO1_PEER else "nccl",
@@ -340,9 +404,12 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
             "clocks": clk,
             "result": {"sum_squares": res.sum_squares, "clip_scale": res.clip_scale},
             "parity": parity,
+            "stress": stress_check,
         }
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
     if parity.get("checked") and not parity["bit_exact"]:
         raise SystemExit(f"rank {rank}: ZeRO-1 parity check against the oracle's golden step "
                          "FAILED")
+    if stress_check.get("checked") and not stress_check["bit_exact"]:
+        raise SystemExit(f"rank {rank}: the 100-step stress trajectory differs from the oracle's")

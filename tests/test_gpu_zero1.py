@@ -176,18 +176,6 @@ def test_zero1_equals_single_replica(table_name, exchange):
         assert all(ms >= 0.0 for ms in times.values()) and sum(times.values()) > 0.0
 
 
-STRESS_STEPS = 100
-STRESS_INJECT = {17: 1, 63: 0}  # step -> rank whose gradient gets an inf
-
-
-def _stress_grads(P: int, table: TensorTable, rank: int, t: int, scale: float) -> np.ndarray:
-    g = synth.grads_student_t(P, 100 + rank, t)
-    bits = synth.bf16_rne_bits((g * np.float32(scale)).astype(np.float32))
-    if STRESS_INJECT.get(t) == rank:
-        synth.inject_nonfinite(bits, t, table.offsets)
-    return bits
-
-
 def _stress_rank(rank, world, port, out_q):
     try:
         from datetime import timedelta
@@ -195,7 +183,7 @@ def _stress_rank(rank, world, port, out_q):
         import torch
         import torch.distributed as dist
 
-        from slmopt import StepOptions, _lib
+        from slmopt import StepOptions, _lib, stress
         from slmopt.zero1 import Zero1Adamw, unique_id
 
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -214,14 +202,17 @@ def _stress_rank(rank, world, port, out_q):
             opt.load_state(st["master"], st["moment"], st["variance"], st["bf16"])
             opt.set_loss_scale(65536.0)
             scale, trace = 65536.0, []
-            for t in range(1, STRESS_STEPS + 1):
-                lr = float(np.float32(_lr(t)))
-                r = opt.step(torch.from_numpy(_stress_grads(P, table, rank, t, scale)).cuda(),
-                             StepOptions(learning_rate=lr, one_based_update=t,
+            for t in range(1, stress.STEPS + 1):
+                bits = stress.rank_gradient(P, table.offsets, rank, t, scale)
+                r = opt.step(torch.from_numpy(bits).cuda(),
+                             StepOptions(learning_rate=stress.learning_rate(t),
+                                         one_based_update=t,
                                          loss_scale_mode=_lib.SCALE_DYNAMIC))
-                trace.append((r.skipped, r.sum_squares, r.clip_scale, r.next_loss_scale))
+                trace.append([int(r.skipped), float(r.sum_squares).hex(),
+                              int(np.float32(r.clip_scale).view(np.uint32)),
+                              float(r.next_loss_scale)])
                 scale = r.next_loss_scale
-            runs.append((trace, _digest(opt.read_state())))
+            runs.append((trace, opt.state_sha256()))
             opt.close()
         out_q.put((rank, {"runs": runs}))
         dist.destroy_process_group()
@@ -229,13 +220,42 @@ def _stress_rank(rank, world, port, out_q):
         out_q.put((rank, {"error": traceback.format_exc()}))
 
 
-def _lr(t: int) -> float:
-    return oracle.schedule_learning_rate(t, 3e-4, 3e-5, 20, 100)[1]
+def _stress_oracle(world: int) -> dict:
+    """The oracle's trajectory: the committed golden for 2/4/8 ranks, else
+    computed here the way tests/golden/make_stress_golden.py does."""
+    import json
+    from pathlib import Path
+
+    from slmopt import stress
+
+    golden = Path(__file__).resolve().parent / "golden" / "stress_golden.json"
+    worlds = json.loads(golden.read_text())["worlds"]
+    if str(world) in worlds:
+        return worlds[str(world)]
+    table = _table("smoke")
+    P = table.parameter_count
+    state = synth.optimizer_state(P, 0)
+    scaler = oracle.Scaler(65536.0, 0)
+    trace = []
+    for t in range(1, stress.STEPS + 1):
+        lr = oracle.schedule_learning_rate(t, stress.PEAK_LR, stress.MIN_LR, stress.WARMUP,
+                                           stress.STEPS)[1]
+        g = oracle.rank_sum_bf16([stress.rank_gradient(P, table.offsets, r, t, scaler.scale)
+                                  for r in range(world)], threads=8)
+        ref = oracle.step(oracle.make_config(lr=lr, t=t, dynamic=True), g, table.offsets,
+                          table.decay, state, scaler, threads=8)
+        trace.append([int(ref.skipped), float(ref.sum_squares).hex(),
+                      int(np.float32(ref.clip_scale).view(np.uint32)),
+                      float(ref.next_loss_scale)])
+    sha = oracle.state_sha256(table.names, table.offsets, table.decay, state)[1]
+    return {"trace": trace, "final_sha256": sha}
 
 
 def test_zero1_stress_trajectory_matches_oracle():
     # warmup 20 then cosine from 3e-4 over 100 steps, Student-t(3) * 1e-3 bf16
     # gradients per rank, dynamic loss scale, +inf injected at two seeded steps
+    from slmopt import stress
+
     n = _gpus()
     if n < 2:
         pytest.skip("needs at least 2 GPUs")
@@ -261,28 +281,15 @@ def test_zero1_stress_trajectory_matches_oracle():
         if p.is_alive():
             p.kill()
     assert len(res) == world, res
+    want = _stress_oracle(world)
     for r, p in res.items():
         assert "error" not in p, p["error"]
         assert p["runs"][0] == p["runs"][1], f"rank {r}: two runs differ"
-    table = _table("smoke")
-    P = table.parameter_count
-    state = synth.optimizer_state(P, 0)
-    scaler = oracle.Scaler(65536.0, 0)
-    trace = res[0]["runs"][0][0]
-    for t in range(1, STRESS_STEPS + 1):
-        g = oracle.rank_sum_bf16([_stress_grads(P, table, r, t, scaler.scale)
-                                  for r in range(world)], threads=8)
-        ref = oracle.step(oracle.make_config(lr=_lr(t), t=t, dynamic=True), g, table.offsets,
-                          table.decay, state, scaler, threads=8)
-        skipped, s, c, nxt = trace[t - 1]
-        assert skipped == ref.skipped, t
-        if not ref.skipped:
-            assert s == ref.sum_squares and np.float32(c) == np.float32(ref.clip_scale), t
-        assert nxt == ref.next_loss_scale, t
-    assert sum(x[0] for x in trace) == len(STRESS_INJECT)
-    want = _digest(state)
-    for r, p in res.items():
-        assert p["runs"][0][1] == want, f"rank {r} final state differs from the oracle"
+        trace, sha = p["runs"][0]
+        for t in range(1, stress.STEPS + 1):
+            assert trace[t - 1] == want["trace"][t - 1], (r, t)
+        assert sum(x[0] for x in trace) == len(stress.INJECT)
+        assert sha == want["final_sha256"], f"rank {r} final state differs from the oracle"
 
 
 def _absent_peer_rank(rank, world, port, out_q):

@@ -226,7 +226,8 @@ int slm_opt_export_weights_f32(slm_opt_handle* h, float* dst_device, uint64_t n,
  *                    finalize + update + weight stores + weight barrier
  *   ZeRO-1 NCCL:     gradient all-to-all, reduce, partials all-gather,
  *                    finalize, update, weight all-gather
- *   slm_opt_apply_update: gradient upload, sequential clip check, update
+ *   slm_opt_apply_update: gradient upload + sequential clip check (overlapped
+ *                    slice by slice for pageable host memory), update
  * A host gradient's upload is not part of any slm_opt_step phase.  The sums
  * describe one entry point: a timed call of the other (slm_opt_step versus
  * slm_opt_apply_update) starts them afresh. */
@@ -256,8 +257,10 @@ int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* str
  * trainer.rs:161) with the reference's own sequential f32 clip scale
  * (gradient_clip_scale, src/model/oracle.rs:486-507, reproduced bit for bit
  * on the device, so the accept / reject decision is the reference's even where
- * that sum drifts from the exact one; ~0.3 s at 135M, an inherently serial
- * sum); the lr must bit-equal
+ * that sum drifts from the exact one; see slm_gradient_clip_scale); from
+ * pageable host memory the gradients travel through a pinned ring filled by
+ * host threads and the check runs slice by slice as they land; the lr must
+ * bit-equal
  * canonical_learning_rate(t) (P12_SCHEDULER_STATE_MISMATCH); AdamW runs with
  * OPT-001's constants and no further clip.  `grads_host` is host f32[n].
  * valid_targets is accepted and unused, as in the reference.  If out_sha256

@@ -5,9 +5,12 @@
 #include "sha256.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
+#include <memory>
 #include <new>
 #include <set>
+#include <thread>
 
 using namespace slmopt;
 
@@ -150,6 +153,7 @@ int allocate_state(slm_opt_handle* h, uint64_t w16_elems) {
   SLM_TRY(cudaMalloc(&h->d_state, sizeof(DeviceStepState)), "cudaMalloc state");
   SLM_TRY(cudaMalloc(&h->d_scaler, sizeof(DeviceScaler)), "cudaMalloc scaler");
   SLM_TRY(cudaMalloc(&h->d_flag, sizeof(uint32_t)), "cudaMalloc flag");
+  SLM_TRY(cudaMalloc(&h->d_seq_carry, sizeof(SeqCarry)), "cudaMalloc clip carry");
   SLM_TRY(cudaMallocHost(&h->h_state, sizeof(DeviceStepState)), "cudaMallocHost state");
   SLM_TRY(cudaMemset(h->master, 0, Ls * sizeof(float)), "memset master");
   SLM_TRY(cudaMemset(h->m1, 0, Ls * sizeof(float)), "memset m1");
@@ -224,9 +228,114 @@ int role_info(slm_opt_handle* h, int role, void** ptr, uint64_t* full_bytes,
   return SLM_OK;
 }
 
+// ---- host gradients in pageable memory ------------------------------------------
+// A cudaMemcpyAsync from pageable memory goes through the driver's own bounce
+// buffer, one buffer at a time, at ~11 GB/s (49 ms for the 541 MB f32
+// gradient the reference hands apply_update).  stage_pageable instead lets
+// several host threads copy consecutive 32 MB slices of the source into a
+// ring of pinned slots while the previous slice's DMA runs on the handle's
+// copy stream, so the host copy and the PCIe transfer overlap.  After each
+// slice's DMA is enqueued, on_slice(offset, bytes, landed) runs on the host
+// with `landed` recorded behind that DMA, so device work on the slice can
+// start while later slices are still on their way.
+bool is_pageable(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return true;
+  }
+  return a.type == cudaMemoryTypeUnregistered;
+}
+
+int ensure_staging(slm_opt_handle* h, size_t bytes) {
+  if (h->staging_bytes >= bytes) return SLM_OK;
+  cudaFree(h->d_staging);
+  h->d_staging = nullptr;
+  h->staging_bytes = 0;
+  const int st = h->cuda(cudaMalloc(&h->d_staging, bytes), "cudaMalloc gradient staging");
+  if (st == SLM_OK) h->staging_bytes = bytes;
+  return st;
+}
+
+template <typename OnSlice>
+int stage_pageable(slm_opt_handle* h, void* dst, const void* src, size_t bytes,
+                   cudaStream_t compute, OnSlice on_slice) {
+  using Ring = slm_opt_handle::PinnedRing;
+  int st;
+  if (!h->copy_stream &&
+      (st = h->cuda(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking),
+                    "copy stream")))
+    return st;
+  for (int k = 0; k < Ring::kSlots; ++k) {
+    if (!h->ring.slot[k] &&
+        (st = h->cuda(cudaMallocHost(&h->ring.slot[k], Ring::kSlotBytes), "pinned staging ring")))
+      return st;
+    if (!h->ring.drained[k] &&
+        (st = h->cuda(cudaEventCreateWithFlags(&h->ring.drained[k], cudaEventDisableTiming),
+                      "staging event")))
+      return st;
+  }
+  // The device buffer may still be read by work enqueued earlier on the
+  // compute stream: the copies wait for it.
+  cudaEvent_t before = nullptr;
+  if ((st = h->cuda(cudaEventCreateWithFlags(&before, cudaEventDisableTiming), "staging event")))
+    return st;
+  st = h->cuda(cudaEventRecord(before, compute), "staging event");
+  if (!st) st = h->cuda(cudaStreamWaitEvent(h->copy_stream, before, 0), "staging wait");
+  cudaEventDestroy(before);
+  if (st) return st;
+
+  const size_t n_slices = (bytes + Ring::kSlotBytes - 1) / Ring::kSlotBytes;
+  const unsigned hw = std::thread::hardware_concurrency();
+  const size_t T = std::min<size_t>(8, std::max<size_t>(1, hw / 2));
+  std::unique_ptr<std::atomic<size_t>[]> parts(new std::atomic<size_t>[n_slices]);
+  for (size_t c = 0; c < n_slices; ++c) parts[c].store(0);
+  std::atomic<size_t> go{0};  // slices whose slot is free to be filled
+  std::atomic<bool> stop{false};
+  auto fill = [&](size_t w) {
+    for (size_t c = 0; c < n_slices; ++c) {
+      while (go.load(std::memory_order_acquire) <= c) {
+        if (stop.load(std::memory_order_acquire)) return;
+        std::this_thread::yield();
+      }
+      const size_t off = c * Ring::kSlotBytes;
+      const size_t len = std::min(Ring::kSlotBytes, bytes - off);
+      const size_t part = (len + T - 1) / T;
+      const size_t lo = std::min(len, w * part), hi = std::min(len, lo + part);
+      if (lo < hi)
+        std::memcpy(static_cast<uint8_t*>(h->ring.slot[c % Ring::kSlots]) + lo,
+                    static_cast<const uint8_t*>(src) + off + lo, hi - lo);
+      parts[c].fetch_add(1, std::memory_order_acq_rel);
+    }
+  };
+  std::vector<std::thread> pool;
+  for (size_t w = 0; w < T; ++w) pool.emplace_back(fill, w);
+  for (size_t c = 0; c < n_slices && st == SLM_OK; ++c) {
+    const int k = int(c % Ring::kSlots);
+    if (h->ring.used[k] &&
+        (st = h->cuda(cudaEventSynchronize(h->ring.drained[k]), "staging slot wait")))
+      break;
+    go.store(c + 1, std::memory_order_release);
+    while (parts[c].load(std::memory_order_acquire) < T) std::this_thread::yield();
+    const size_t off = c * Ring::kSlotBytes;
+    const size_t len = std::min(Ring::kSlotBytes, bytes - off);
+    st = h->cuda(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, h->ring.slot[k], len,
+                                 cudaMemcpyHostToDevice, h->copy_stream),
+                 "gradient upload");
+    if (!st) st = h->cuda(cudaEventRecord(h->ring.drained[k], h->copy_stream), "staging event");
+    if (st) break;
+    h->ring.used[k] = true;
+    st = on_slice(off, len, h->ring.drained[k]);
+  }
+  stop.store(true, std::memory_order_release);
+  for (auto& th : pool) th.join();
+  return st;
+}
+
 // Stage the gradient: device pointers are used in place (16-byte alignment
 // required for the vector loads), host pointers are copied into a staging
-// buffer on the step's stream.
+// buffer ahead of the step's work on its stream (pinned memory with one
+// asynchronous copy, pageable memory through stage_pageable).
 int stage_grads(slm_opt_handle* h, const void* grads, int dtype, int memory, cudaStream_t s,
                 const void** dev_grads) {
   const size_t esize = dtype == SLM_DTYPE_F32 ? 4 : 2;
@@ -238,16 +347,17 @@ int stage_grads(slm_opt_handle* h, const void* grads, int dtype, int memory, cud
     return SLM_OK;
   }
   if (memory != SLM_MEMORY_HOST) return h->err(SLM_ERR_INVALID_ARGUMENT, "unknown memory kind");
-  if (h->staging_bytes < bytes) {
-    cudaFree(h->d_staging);
-    h->d_staging = nullptr;
-    h->staging_bytes = 0;
-    int st = h->cuda(cudaMalloc(&h->d_staging, bytes), "cudaMalloc gradient staging");
-    if (st) return st;
-    h->staging_bytes = bytes;
+  int st = ensure_staging(h, bytes);
+  if (st) return st;
+  if (is_pageable(grads) && bytes > slm_opt_handle::PinnedRing::kSlotBytes) {
+    st = stage_pageable(h, h->d_staging, grads, bytes, s,
+                        [&](size_t, size_t, cudaEvent_t landed) {
+                          return h->cuda(cudaStreamWaitEvent(s, landed, 0), "upload wait");
+                        });
+  } else {
+    st = h->cuda(cudaMemcpyAsync(h->d_staging, grads, bytes, cudaMemcpyHostToDevice, s),
+                 "gradient upload");
   }
-  int st = h->cuda(cudaMemcpyAsync(h->d_staging, grads, bytes, cudaMemcpyHostToDevice, s),
-                   "gradient upload");
   if (st) return st;
   *dev_grads = h->d_staging;
   return SLM_OK;
@@ -481,7 +591,15 @@ int slm_opt_destroy(slm_opt_handle* h) {
   cudaFree(h->d_state);
   cudaFree(h->d_scaler);
   cudaFree(h->d_flag);
+  cudaFree(h->d_seq_carry);
   cudaFree(h->d_staging);
+  for (int k = 0; k < slm_opt_handle::PinnedRing::kSlots; ++k) {
+    if (h->ring.drained[k]) {
+      cudaEventSynchronize(h->ring.drained[k]);
+      cudaEventDestroy(h->ring.drained[k]);
+    }
+    if (h->ring.slot[k]) cudaFreeHost(h->ring.slot[k]);
+  }
   if (h->copy_stream) {
     cudaStreamSynchronize(h->copy_stream);
     cudaStreamDestroy(h->copy_stream);
@@ -882,13 +1000,13 @@ int slm_opt_phase_times(slm_opt_handle* h, double* mean_ms, uint32_t capacity,
 
 const char* slm_opt_phase_name(const slm_opt_handle* h, uint32_t phase) {
   static const char* const kSingle[] = {"norm pass", "update"};
-  static const char* const kApply[] = {"gradient upload", "sequential clip check", "update"};
+  static const char* const kApply[] = {"gradient upload + sequential clip check", "update"};
   static const char* const kPeer[] = {"gradient barrier + peer reduce",
                                       "finalize + update + weight stores + weight barrier"};
   static const char* const kNccl[] = {"gradient all-to-all", "reduce", "partials all-gather",
                                       "finalize", "update", "weight all-gather"};
   if (!h) return nullptr;
-  if (h->timer.kind == kApplyUpdateCall) return phase < 3 ? kApply[phase] : nullptr;
+  if (h->timer.kind == kApplyUpdateCall) return phase < 2 ? kApply[phase] : nullptr;
   if (!h->sharded()) return phase < 2 ? kSingle[phase] : nullptr;
   if (h->exchange == SLM_ZERO1_PEER) return phase < 2 ? kPeer[phase] : nullptr;
   return phase < 6 ? kNccl[phase] : nullptr;
@@ -928,14 +1046,34 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
   const void* dev = nullptr;
   int st = phase_begin(h, s);
   if (st) return st;
-  if ((st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev))) return st;
-  if ((st = phase_mark(h, s))) return st;
   // Re-verification first (trainer.rs:250-260), with the reference's own
   // sequential f32 clip scale so that the accept / reject decision is the
-  // reference's; nothing is written on failure.
-  if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s),
-                    "clip check kernel")))
-    return st;
+  // reference's; nothing is written on failure.  From pageable memory the
+  // check runs slice by slice as the slices land, overlapping the upload.
+  const size_t bytes = h->P * sizeof(float);
+  if (is_pageable(grads_host) && bytes > slm_opt_handle::PinnedRing::kSlotBytes) {
+    if ((st = ensure_staging(h, bytes))) return st;
+    float* staged = static_cast<float*>(h->d_staging);
+    const SeqClipOut out{h->d_state, nullptr, nullptr, nullptr};
+    st = stage_pageable(h, staged, grads_host, bytes, s,
+                        [&](size_t off, size_t len, cudaEvent_t landed) {
+                          int r = h->cuda(cudaStreamWaitEvent(s, landed, 0), "upload wait");
+                          if (r) return r;
+                          const uint64_t e0 = off / sizeof(float), ne = len / sizeof(float);
+                          return h->cuda(launch_sequential_clip(staged + e0, ne, out,
+                                                                &h->d_state->kernel_error, s,
+                                                                h->d_seq_carry, e0 != 0,
+                                                                e0 + ne == h->P),
+                                         "clip check kernel");
+                        });
+    if (st) return st;
+    dev = staged;
+  } else {
+    if ((st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev))) return st;
+    if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s),
+                      "clip check kernel")))
+      return st;
+  }
   if ((st = phase_mark(h, s))) return st;
   DeviceStepState ds;
   if ((st = read_state(h, s, &ds))) return st;

@@ -121,6 +121,18 @@ struct slm_opt_handle {
   cudaStream_t copy_stream = nullptr;
   int next_up = 0;
 
+  // Pageable host gradients (slm_opt_apply_update's slice, slm_opt_step on
+  // host memory that is not pinned) travel through a ring of pinned slots
+  // filled by host threads, one DMA per slot on copy_stream (stage_pageable).
+  struct PinnedRing {
+    static constexpr int kSlots = 3;
+    static constexpr size_t kSlotBytes = size_t(32) << 20;  // 8M f32: whole clip windows
+    void* slot[kSlots] = {};
+    cudaEvent_t drained[kSlots] = {};  // the slot's last DMA has read it
+    bool used[kSlots] = {};
+  } ring;
+  slmopt::SeqCarry* d_seq_carry = nullptr;  // sequential clip's state between slices
+
   // ---- ZeRO-1 (world > 1) ---------------------------------------------------
   int rank = 0, world = 1;
   void* comm = nullptr;            // ncclComm_t

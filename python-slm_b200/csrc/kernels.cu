@@ -1293,7 +1293,7 @@ __device__ __forceinline__ uint32_t seq_increment(float q, int32_t E, bool& tie)
 
 __global__ void __launch_bounds__(kSeqThreads, 1)
     sequential_clip_kernel(const float* __restrict__ g, uint64_t n, SeqClipOut out,
-                           uint32_t* kernel_error) {
+                           uint32_t* kernel_error, SeqCarry* carry, int resume, int finish) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t warp_val[kSeqThreads / 32];
   __shared__ uint32_t warp_stop[kSeqThreads / 32];
@@ -1301,15 +1301,26 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
   __shared__ uint32_t s_m, s_restart, s_sum_bad, s_stop, s_total;
   __shared__ uint32_t s_fast_total[2], s_fast_tie[2];
   __shared__ float s_sum_bits;
+  __shared__ uint32_t s_gbad_before;
   const float* ring = reinterpret_cast<const float*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kSeqStages) * kSeqWindowBytes);
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   if (t == 0) {
     for (uint32_t s = 0; s < kSeqStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    s_E = -149;
-    s_m = 0u;
-    s_sum_bad = 0u;
+    if (resume) {  // continue the sum of the slices before this one
+      s_E = carry->E;
+      s_m = carry->m;
+      s_sum_bad = carry->sum_bad;
+      s_sum_bits = carry->sum_bits;
+      s_gbad_before = carry->gbad;
+    } else {
+      s_E = -149;
+      s_m = 0u;
+      s_sum_bad = 0u;
+      s_sum_bits = 0.0f;
+      s_gbad_before = 0u;
+    }
   }
   __syncthreads();
   const uint64_t n_full = n / kSeqWindow;
@@ -1482,10 +1493,18 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
   if (!ok && t == 0)
     for (uint64_t u = issued > kSeqStages ? issued - kSeqStages : 0; u < issued; ++u)
       mbar_wait(&full[u % kSeqStages], uint32_t(u / kSeqStages) & 1u);
-  const int any_bad = __syncthreads_or(gbad ? 1 : 0);
+  const int any_bad = __syncthreads_or(gbad ? 1 : 0) || s_gbad_before;
   if (t != 0) return;
   if (!ok) {
     atomicOr(kernel_error, 1u);
+    return;
+  }
+  if (!finish) {  // hand the running sum to the launch for the next slice
+    carry->E = s_E;
+    carry->m = s_m;
+    carry->sum_bad = s_sum_bad;
+    carry->sum_bits = s_sum_bits;
+    carry->gbad = any_bad ? 1u : 0u;
     return;
   }
   const float sum = s_sum_bad ? s_sum_bits : seq_compose(s_E, s_m);
@@ -2355,12 +2374,15 @@ cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* s
 }
 
 cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
-                                   uint32_t* kernel_error, cudaStream_t stream) {
+                                   uint32_t* kernel_error, cudaStream_t stream, SeqCarry* carry,
+                                   bool resume, bool finish) {
+  if ((resume || !finish) && carry == nullptr) return cudaErrorInvalidValue;
   const int bytes = int(kSeqStages * kSeqWindowBytes + kBarrierBytes);
   cudaError_t e = cudaFuncSetAttribute(sequential_clip_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
-  sequential_clip_kernel<<<1, kSeqThreads, bytes, stream>>>(g, n, out, kernel_error);
+  sequential_clip_kernel<<<1, kSeqThreads, bytes, stream>>>(g, n, out, kernel_error, carry,
+                                                            resume ? 1 : 0, finish ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -210,8 +210,23 @@ struct SeqClipOut {
   float* clip;
   int32_t* status;
 };
+// The running state of the sequential sum between launches over consecutive
+// slices (each slice but the last a whole number of 8,192-term windows).
+struct SeqCarry {
+  int32_t E;          // the sum is m * 2^E
+  uint32_t m;
+  uint32_t sum_bad;   // the sum became non-finite (sum_bits holds it)
+  float sum_bits;
+  uint32_t gbad;      // a non-finite gradient was seen
+  uint32_t reserved[3];
+};
+constexpr uint64_t kSeqSliceAlign = 8192;  // terms per window of the sequential sum
+// resume: start from *carry (else from zero); finish: write the result to
+// `out` (else save the running state to *carry).
 cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
-                                   uint32_t* kernel_error, cudaStream_t stream);
+                                   uint32_t* kernel_error, cudaStream_t stream,
+                                   SeqCarry* carry = nullptr, bool resume = false,
+                                   bool finish = true);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

@@ -750,3 +750,53 @@ def test_gradient_clip_scale_at_production_width(torch):
     assert np.float32(got_sum).view(np.uint32) == np.float32(want_sum).view(np.uint32)
     assert got_clip == 1.0
     assert got_sum < 0.7 * 0.81  # the drift the exact sum would not show
+
+
+# ---- pageable host gradients through the pinned ring (several 32 MB slices) --------------
+def test_pageable_host_gradients_at_135m_equal_device_gradients(torch):
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    n = table.parameter_count
+    grads = synth.grads_bf16(n, 6)  # numpy: pageable, 270 MB = 9 slices
+    opts = StepOptions(one_based_update=4, static_loss_scale=65536.0)
+    r1, g1, _, _ = run_both(torch, table, grads, opts, seed=6)
+    r2, g2, ores, ost = run_both(torch, table, grads, opts, seed=6, host_grads=True)
+    check_equal(r2, g2, ores, ost)
+    assert r1.sum_squares == r2.sum_squares
+    for key in g1:
+        assert_same_bits(g1[key], g2[key], key)
+
+
+def test_apply_update_rejects_late_slices_like_the_reference(torch):
+    # The strict path checks slice by slice as the upload lands: a non-finite
+    # value in slice 15 of 17, or a gradient too large for the 0.95 clip
+    # tolerance, must still be refused with nothing written.
+    table = TensorTable.from_dimensions(GqaDimensions.canonical())
+    n = table.parameter_count
+    g = synth.grads_f32(n, 9)
+    g *= np.float32(0.5 / float(np.sqrt(np.sum(g.astype(np.float64) ** 2))))
+    state = synth.optimizer_state(n, 9)
+    lr = oracle.canonical_learning_rate(1)[1]
+    bad = g.copy()
+    bad[125_000_003] = np.inf
+    big = (g * np.float32(30.0)).astype(np.float32)
+    with B200Adamw(table) as opt:
+        opt.load_state(state["master"], state["moment"], state["variance"], state["bf16"])
+        for grads, want in ((bad, oracle.MODEL_GRADIENT_NONFINITE),
+                            (big, oracle.P12_OPTIMIZER_GRADIENT_INVALID)):
+            assert oracle.apply_normalized_clipped_gradients(
+                grads, lr, 1, table.offsets, table.decay,
+                {k: v.copy() for k, v in state.items()})[0] == want
+            with pytest.raises(SlmError) as e:
+                opt.apply_normalized_clipped_gradients(grads, lr, 1, with_sha=False)
+            assert e.value.status == want
+        got = opt.read_state()
+        for key in ("master", "moment", "variance", "bf16"):
+            assert_same_bits(got[key], state[key], key)
+        # and a good one afterwards still matches the oracle bit for bit
+        opt.apply_normalized_clipped_gradients(g, lr, 1, with_sha=False)
+        got = opt.read_state()
+    ost = {k: v.copy() for k, v in state.items()}
+    assert oracle.apply_normalized_clipped_gradients(g, lr, 1, table.offsets, table.decay,
+                                                     ost)[0] == oracle.OK
+    for key in ("master", "moment", "variance", "bf16"):
+        assert_same_bits(got[key], ost[key], key)

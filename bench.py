@@ -304,9 +304,26 @@ def time_apply_update(table, state, calls: int = 2) -> dict:
         phases, n = opt.phase_times()
         opt.phase_timing(False)
     times = times[1:]
+    # The sequential clip check alone on a device-resident gradient
+    # (slm_gradient_clip_scale; CUDA events on the launching stream).
+    import ctypes
+
+    dev = torch.from_numpy(g).cuda()
+    out = torch.zeros(ctypes.sizeof(_lib.ClipResult), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    _lib.check(lib.slm_gradient_clip_scale(dev.data_ptr(), P, out.data_ptr(), stream.cuda_stream))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        _lib.check(lib.slm_gradient_clip_scale(dev.data_ptr(), P, out.data_ptr(),
+                                               stream.cuda_stream))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clip_ms = e0.elapsed_time(e1) / 3
     return {"api": "slm_opt_apply_update", "params": P, "calls": len(times),
             "ms_per_call": statistics.median(times),
             "phases_ms": phases, "phase_calls": n,
+            "clip_scale_alone_ms": clip_ms,
             "note": "synchronous wall clock; host f32 gradients (pageable), the reference's "
                     "sequential f32 clip re-verification on the device, AdamW; state hash off"}
 

@@ -1598,7 +1598,7 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
 // Every wait is bounded by timeout_ns; after a wait of a step has given up
 // (kernel_error), later waits of the step return at once.
 #ifndef SLM_PEER_LOADS
-#define SLM_PEER_LOADS 0
+#define SLM_PEER_LOADS 1
 #endif
 #ifndef SLM_PEER_STAGES
 #define SLM_PEER_STAGES 3
@@ -1781,17 +1781,17 @@ __global__ void __launch_bounds__(kTreeThreads)
     ok = wait_epoch(pt.flags[rank] + kSlotGrads * kMaxRanks + threadIdx.x, epoch, st,
                     timeout_ns);
     if (!ok) atomicOr(&st->kernel_error, 2u);
+    // Acquire: the peer's gradients were published before its flag.  The
+    // block barrier below orders the other threads' reads after this fence;
+    // the bulk copy engine reads through the async proxy, hence its fence.
+    __threadfence_system();
+    if (kBatch == 0) asm volatile("fence.proxy.async;" ::: "memory");
   }
   if (kBatch == 0 && threadIdx.x == 0) {
     for (uint32_t s = 0; s < kPeerStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   ok = __syncthreads_or(ok ? 0 : 1) == 0;
-  // The peers' gradients (published before their flags) are read by the bulk
-  // copy engine: order the flag observations before those reads.
-  __threadfence_system();
-  if (threadIdx.x == 0) asm volatile("fence.proxy.async;" ::: "memory");
-  __syncthreads();
   const ScaleInfo sc = decode_scale(fp.dynamic ? scaler->scale : fp.static_scale);
   const uint64_t base = uint64_t(c) * kChunkElems;
   double acc = 0.0;
@@ -1955,9 +1955,9 @@ __global__ void __launch_bounds__(kBulkThreads)
     if (wok && t < static_cast<unsigned>(world)) {
       wok = wait_epoch(pt.flags[rank] + kSlotPartials * kMaxRanks + t, epoch, st, timeout_ns);
       if (!wok) atomicOr(&st->kernel_error, 2u);
+      __threadfence_system();  // acquire rank t's partials; the barrier orders the others
     }
     if (consumers_all(wok)) {
-      __threadfence_system();
       const PartialsView view{pt.gathered[rank], per_rank, per_rank + 1};
       const double sum =
           consumer_fold(finalize_lane_sum(view, uint32_t(world) * per_rank, t), warp_sums);
@@ -2023,7 +2023,9 @@ __global__ void __launch_bounds__(kBulkThreads)
       }
     }
   }
-  __threadfence_system();  // this thread's peer stores before the block counts as done
+  // Peer stores before the block counts as done: thread 0's bulk stores, and
+  // the ragged tail's plain stores in block 0.
+  if (blockIdx.x == 0 || threadIdx.x == 0) __threadfence_system();
   if (__syncthreads_or(ok ? 0 : 1) && threadIdx.x == kBulkConsumers)
     for (uint32_t u = i > kBulkStages ? i - kBulkStages : 0u; u < i; ++u)
       mbar_wait(&full_bar[u % kBulkStages], (u / kBulkStages) & 1u);

@@ -22,6 +22,9 @@ from .layout import TensorTable
 from .optimizer import B200Adamw
 
 CHUNK = 65536
+# Peer-copy bandwidth per direction between two B200s over NVLink 5 /
+# NVSwitch, measured with cudaMemcpyPeerAsync (bench.py --nvlink-peak).
+NVLINK_PEAK_GBS = 770.0
 
 
 @dataclass(frozen=True)
@@ -200,7 +203,7 @@ def _zero1_parity(opt, table, state, grads, dev, opts, rank, world, args) -> dic
 
 
 def _zero1_stress(rank: int, world: int) -> dict:
-    """BASELINE's 100-step stress run (collective), checked against the
+    """The 100-update dynamic-loss-scale stress run (collective), checked against the
     oracle's trajectory for this rank count (tests/golden/stress_golden.json):
     per update the skip decision, the f64 norm's bits, the clip's bits and the
     next loss scale, and the final state's SHA-256.  Smoke tensor list, inputs
@@ -388,9 +391,11 @@ def bench_main(args, metric, unit, workload_config, clock_sampler, hbm_peak) -> 
             "data": "synthetic (seeded numpy Philox normals; rank r uses seed r)",
             "config": workload_config(args, world, P, len(table)),
             "roofline": {"bound": "nvlink", "achieved": nvlink_bytes / (ms * 1e-3) / 1e9,
-                         "peak": 770.0, "unit": "GB/s",
-                         "frac": nvlink_bytes / (ms * 1e-3) / 1e9 / 770.0, "traffic": None,
-                         "peak_source": "measured peer copy per direction (pool figure)",
+                         "peak": NVLINK_PEAK_GBS, "unit": "GB/s",
+                         "frac": nvlink_bytes / (ms * 1e-3) / 1e9 / NVLINK_PEAK_GBS,
+                         "traffic": None,
+                         "peak_source": "measured peer copy per direction "
+                                        "(bench.py --nvlink-peak)",
                          "nvlink_bytes_per_rank": nvlink_bytes,
                          "hbm_peak_gbs": peak, "hbm_peak_source": peak_kind},
             "e2e": {"value": P / (e2e_ms * 1e-3), "unit": unit,

@@ -304,22 +304,39 @@ def time_apply_update(table, state, calls: int = 2) -> dict:
         phases, n = opt.phase_times()
         opt.phase_timing(False)
     times = times[1:]
-    # The sequential clip check alone on a device-resident gradient
-    # (slm_gradient_clip_scale; CUDA events on the launching stream).
+    # The sequential clip check alone on a device-resident gradient, in both
+    # forms: one CTA streaming the terms (slm_gradient_clip_scale) and the
+    # window summaries on every SM chained by one CTA (slm_gradient_clip_scale_ws).
+    # CUDA events on the launching stream.
     import ctypes
 
     dev = torch.from_numpy(g).cuda()
     out = torch.zeros(ctypes.sizeof(_lib.ClipResult), dtype=torch.uint8, device="cuda")
+    ws_bytes = int(lib.slm_gradient_clip_workspace_bytes(P))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
-    _lib.check(lib.slm_gradient_clip_scale(dev.data_ptr(), P, out.data_ptr(), stream.cuda_stream))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(3):
+
+    def one_cta():
         _lib.check(lib.slm_gradient_clip_scale(dev.data_ptr(), P, out.data_ptr(),
                                                stream.cuda_stream))
-    e1.record(stream)
-    torch.cuda.synchronize()
-    clip_ms = e0.elapsed_time(e1) / 3
+
+    def all_sms():
+        _lib.check(lib.slm_gradient_clip_scale_ws(dev.data_ptr(), P, ws.data_ptr(), ws_bytes,
+                                                  out.data_ptr(), stream.cuda_stream))
+
+    clip_ms = {}
+    results = {}
+    for name, fn, reps in (("one_cta", one_cta, 3), ("all_sms", all_sms, 10)):
+        fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clip_ms[name] = e0.elapsed_time(e1) / reps
+        results[name] = bytes(out.cpu().numpy().tobytes())
+    clip_ms["same_bits"] = results["one_cta"] == results["all_sms"]
     return {"api": "slm_opt_apply_update", "params": P, "calls": len(times),
             "ms_per_call": statistics.median(times),
             "phases_ms": phases, "phase_calls": n,

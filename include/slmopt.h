@@ -282,7 +282,16 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
  * `stream`): status 0, MODEL_GRADIENT_NONFINITE (a gradient is inf or NaN;
  * takes precedence, as in the reference) or MODEL_GRADIENT_NORM_NONFINITE
  * (the sum overflowed); kernel_error 1 if the kernel's copy pipeline stalled
- * (never expected).  Allocates nothing. */
+ * (never expected).  Allocates nothing; one CTA streams the n terms
+ * (about 0.25 ms per million).  slm_gradient_clip_scale_ws gives the same
+ * bits with every SM: workspace_device (device memory, 16-byte aligned, at
+ * least slm_gradient_clip_workspace_bytes(n) bytes -- 29 per 8,192 gradients,
+ * rounded up to 16) receives per-window summaries computed in parallel (the
+ * window's exact f64 sum and, for the few binades the running sum can be in
+ * there, its integer ulp total and whether an add ties), which one CTA then
+ * chains in order, adding a window term by term only where no summary fits.
+ * A workspace that is too small or misaligned is INVALID_ARGUMENT; NULL
+ * selects the single-CTA form. */
 typedef struct slm_clip_result {
     float sum_squares;     /* the reference's sequential f32 sum */
     float clip_scale;
@@ -291,6 +300,10 @@ typedef struct slm_clip_result {
 } slm_clip_result;
 int slm_gradient_clip_scale(const float* grads_device, uint64_t n, slm_clip_result* out_device,
                             void* stream);
+uint64_t slm_gradient_clip_workspace_bytes(uint64_t n);
+int slm_gradient_clip_scale_ws(const float* grads_device, uint64_t n, void* workspace_device,
+                               uint64_t workspace_bytes, slm_clip_result* out_device,
+                               void* stream);
 
 /* ---- micro-batch accumulation ---------------------------------------------------
  * The reference sums each micro-batch's fp32 gradient into a host accumulator

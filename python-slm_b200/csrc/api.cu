@@ -154,6 +154,8 @@ int allocate_state(slm_opt_handle* h, uint64_t w16_elems) {
   SLM_TRY(cudaMalloc(&h->d_scaler, sizeof(DeviceScaler)), "cudaMalloc scaler");
   SLM_TRY(cudaMalloc(&h->d_flag, sizeof(uint32_t)), "cudaMalloc flag");
   SLM_TRY(cudaMalloc(&h->d_seq_carry, sizeof(SeqCarry)), "cudaMalloc clip carry");
+  h->seq_ws_bytes = seq_clip_workspace_bytes(h->P);
+  SLM_TRY(cudaMalloc(&h->d_seq_ws, h->seq_ws_bytes), "cudaMalloc clip workspace");
   SLM_TRY(cudaMallocHost(&h->h_state, sizeof(DeviceStepState)), "cudaMallocHost state");
   SLM_TRY(cudaMemset(h->master, 0, Ls * sizeof(float)), "memset master");
   SLM_TRY(cudaMemset(h->m1, 0, Ls * sizeof(float)), "memset m1");
@@ -592,6 +594,7 @@ int slm_opt_destroy(slm_opt_handle* h) {
   cudaFree(h->d_scaler);
   cudaFree(h->d_flag);
   cudaFree(h->d_seq_carry);
+  cudaFree(h->d_seq_ws);
   cudaFree(h->d_staging);
   for (int k = 0; k < slm_opt_handle::PinnedRing::kSlots; ++k) {
     if (h->ring.drained[k]) {
@@ -752,9 +755,24 @@ int slm_grad_accumulate(float* acc_device, const void* micro_device, int dtype, 
   return SLM_OK;
 }
 
+uint64_t slm_gradient_clip_workspace_bytes(uint64_t n) { return seq_clip_workspace_bytes(n); }
+
 int slm_gradient_clip_scale(const float* grads_device, uint64_t n, slm_clip_result* out_device,
                             void* stream) {
+  return slm_gradient_clip_scale_ws(grads_device, n, nullptr, 0, out_device, stream);
+}
+
+int slm_gradient_clip_scale_ws(const float* grads_device, uint64_t n, void* workspace_device,
+                               uint64_t workspace_bytes, slm_clip_result* out_device,
+                               void* stream) {
   if ((!grads_device && n) || !out_device) return fail(SLM_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (workspace_device) {
+    if (reinterpret_cast<uintptr_t>(workspace_device) % 16 != 0)
+      return fail(SLM_ERR_INVALID_ARGUMENT, "the workspace must be 16-byte aligned");
+    if (workspace_bytes < seq_clip_workspace_bytes(n))
+      return fail(SLM_ERR_INVALID_ARGUMENT,
+                  "the workspace is smaller than slm_gradient_clip_workspace_bytes(n)");
+  }
   if (reinterpret_cast<uintptr_t>(grads_device) % 16 != 0)
     return fail(SLM_ERR_INVALID_ARGUMENT, "gradients must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(out_device) % alignof(slm_clip_result) != 0)
@@ -764,7 +782,8 @@ int slm_gradient_clip_scale(const float* grads_device, uint64_t n, slm_clip_resu
   if (e == cudaSuccess) {
     const SeqClipOut out{nullptr, &out_device->sum_squares, &out_device->clip_scale,
                          &out_device->status};
-    e = launch_sequential_clip(grads_device, n, out, &out_device->kernel_error, s);
+    e = launch_sequential_clip(grads_device, n, out, &out_device->kernel_error, s, nullptr,
+                               false, true, workspace_device, size_t(workspace_bytes));
   }
   if (e != cudaSuccess)
     return fail(SLM_ERR_CUDA, std::string("clip scale kernel: ") + cudaGetErrorString(e));
@@ -1063,14 +1082,16 @@ int slm_opt_apply_update(slm_opt_handle* h, const float* grads_host, uint64_t n,
                           return h->cuda(launch_sequential_clip(staged + e0, ne, out,
                                                                 &h->d_state->kernel_error, s,
                                                                 h->d_seq_carry, e0 != 0,
-                                                                e0 + ne == h->P),
+                                                                e0 + ne == h->P, h->d_seq_ws,
+                                                                h->seq_ws_bytes),
                                          "clip check kernel");
                         });
     if (st) return st;
     dev = staged;
   } else {
     if ((st = stage_grads(h, grads_host, SLM_DTYPE_F32, SLM_MEMORY_HOST, s, &dev))) return st;
-    if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s),
+    if ((st = h->cuda(launch_reference_clip(static_cast<const float*>(dev), h->P, h->d_state, s,
+                                            h->d_seq_ws, h->seq_ws_bytes),
                       "clip check kernel")))
       return st;
   }

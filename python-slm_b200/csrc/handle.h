@@ -132,6 +132,8 @@ struct slm_opt_handle {
     bool used[kSlots] = {};
   } ring;
   slmopt::SeqCarry* d_seq_carry = nullptr;  // sequential clip's state between slices
+  void* d_seq_ws = nullptr;                 // its window summaries (all P gradients)
+  size_t seq_ws_bytes = 0;
 
   // ---- ZeRO-1 (world > 1) ---------------------------------------------------
   int rank = 0, world = 1;

@@ -1291,36 +1291,192 @@ __device__ __forceinline__ uint32_t seq_increment(float q, int32_t E, bool& tie)
   return d < 0 ? (1u << 25) : (d == 0 ? Q : r);
 }
 
+// Shared state of the sequential sum within one CTA.
+struct SeqShared {
+  uint32_t warp_val[kSeqThreads / 32];
+  uint32_t warp_stop[kSeqThreads / 32];
+  int32_t E;           // the running sum is m * 2^E ...
+  uint32_t m;
+  uint32_t sum_bad;    // ... unless it became non-finite (then sum_bits holds it)
+  float sum_bits;
+  uint32_t restart, stop, total;
+  uint32_t fast_total[2], fast_tie[2];
+  uint32_t gbad_before;  // a non-finite gradient in an earlier slice
+};
+
+__device__ __forceinline__ void seq_begin(SeqShared& sh, const SeqCarry* carry, int resume) {
+  if (resume) {  // continue the sum of the slices before this one
+    sh.E = carry->E;
+    sh.m = carry->m;
+    sh.sum_bad = carry->sum_bad;
+    sh.sum_bits = carry->sum_bits;
+    sh.gbad_before = carry->gbad;
+  } else {
+    sh.E = -149;
+    sh.m = 0u;
+    sh.sum_bad = 0u;
+    sh.sum_bits = 0.0f;
+    sh.gbad_before = 0u;
+  }
+}
+
+// Adds one window's terms (thread t holds terms 8t..8t+7 as q[], already
+// squared) to the running sum, exactly: a block-wide prefix of increments
+// finds the first term that ties or leaves the binade, the prefix before it
+// is applied, that term is added with a real f32 add, and the rest of the
+// window is redone with the new binade.  Called by all threads of the CTA.
+__device__ __forceinline__ void seq_window_exact(SeqShared& sh, const float (&q)[kSeqPer]) {
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  uint32_t* warp_val = sh.warp_val;
+  uint32_t* warp_stop = sh.warp_stop;
+  uint32_t start = 0;  // first term of the window not yet added
+  for (;;) {           // block-uniform: every value below is read after a barrier
+    if (sh.sum_bad) break;
+    const int32_t E = sh.E;
+    const uint32_t m = sh.m;
+    uint32_t pre[kSeqPer], run = 0, stop = kNoStop;
+#pragma unroll
+    for (uint32_t j = 0; j < kSeqPer; ++j) {
+      const uint32_t idx = 8 * t + j;
+      bool tie = false;
+      const uint32_t r = idx < start ? 0u : seq_increment(q[j], E, tie);
+      run += r;
+      pre[j] = run;
+      if (tie && stop == kNoStop) stop = idx;
+    }
+    // exclusive prefix of the thread totals over the block
+    uint32_t incl = run;
+#pragma unroll
+    for (uint32_t off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFull, incl, off);
+      if (lane >= off) incl += y;
+    }
+    if (lane == 31) warp_val[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t v = warp_val[lane];
+#pragma unroll
+      for (uint32_t off = 1; off < 32; off <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, v, off);
+        if (lane >= off) v += y;
+      }
+      warp_val[lane] = v;
+    }
+    __syncthreads();
+    const uint32_t excl = (incl - run) + (warp ? warp_val[warp - 1] : 0u);
+    const uint32_t total = warp_val[31];
+    // first term whose running sum would leave the binade (exact up to it)
+#pragma unroll
+    for (uint32_t j = 0; j < kSeqPer; ++j) {
+      const uint32_t idx = 8 * t + j;
+      if (idx >= start && idx < stop && uint64_t(m) + excl + pre[j] >= (1ull << 24)) stop = idx;
+    }
+    const uint32_t wmin = __reduce_min_sync(kFull, stop);
+    if (lane == 0) warp_stop[warp] = wmin;
+    __syncthreads();
+    if (warp == 0) {
+      const uint32_t v = __reduce_min_sync(kFull, warp_stop[lane]);
+      if (lane == 0) {
+        sh.stop = v;
+        sh.total = total;
+      }
+    }
+    __syncthreads();
+    const uint32_t first = sh.stop;
+    if (first == kNoStop) {  // the whole rest of the window stays in the binade
+      if (t == 0) sh.m = m + sh.total;
+      __syncthreads();
+      break;
+    }
+    if (first >= 8 * t && first < 8 * t + kSeqPer) {  // the owner of the stopping term
+      const uint32_t j0 = first - 8 * t;
+      uint32_t before = excl;
+      float qj = 0.0f;
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {  // no dynamic register indexing
+        if (j + 1 == j0) before += pre[j];
+        if (j == j0) qj = q[j];
+      }
+      const float sum = __fadd_rn(seq_compose(E, m + before), qj);
+      if (!finite_f32(sum)) {
+        sh.sum_bad = 1u;
+        sh.sum_bits = sum;
+      } else {
+        int32_t E2;
+        uint32_t m2;
+        seq_decompose(sum, E2, m2);
+        sh.E = E2;
+        sh.m = m2;
+      }
+      sh.restart = first + 1;
+    }
+    __syncthreads();
+    start = sh.restart;
+    if (start >= kSeqWindow) break;
+  }
+}
+
+// Thread 0: the result (or, between slices, the running state).
+__device__ __forceinline__ void seq_store(const SeqShared& sh, bool any_bad, bool ok,
+                                          const SeqClipOut& out, uint32_t* kernel_error,
+                                          SeqCarry* carry, int finish) {
+  if (!ok) {
+    atomicOr(kernel_error, 1u);
+    return;
+  }
+  if (!finish) {  // hand the running sum to the launch for the next slice
+    carry->E = sh.E;
+    carry->m = sh.m;
+    carry->sum_bad = sh.sum_bad;
+    carry->sum_bits = sh.sum_bits;
+    carry->gbad = any_bad ? 1u : 0u;
+    return;
+  }
+  const float sum = sh.sum_bad ? sh.sum_bits : seq_compose(sh.E, sh.m);
+  int32_t status = kStatusOk;
+  float clip = 1.0f;
+  if (any_bad) {
+    status = kStatusGradientNonfinite;
+  } else if (!finite_f32(sum)) {
+    status = kStatusNormNonfinite;
+  } else if (sum != 0.0f) {
+    const float c = __fdiv_rn(1.0f, __fsqrt_rn(sum));
+    clip = c < 1.0f ? c : 1.0f;
+  }
+  if (out.st) {
+    DeviceStepState* st = out.st;
+    st->sum_squares = double(sum);
+    st->grad_norm = double(__fsqrt_rn(sum));
+    st->clip_scale = clip;
+    st->clip_apply = 1.0f;  // the gradients arrive clipped
+    st->loss_scale_used = 1.0f;
+    st->next_loss_scale = 1.0f;
+    st->skipped = status == kStatusOk ? 0u : 1u;
+    st->nonfinite = status == kStatusOk ? 0u : 1u;
+    st->result_nonfinite = 0u;
+    st->rejected = 0u;
+    st->status = status;
+  } else {
+    *out.sum = sum;
+    *out.clip = clip;
+    *out.status = status;
+  }
+}
+
+// One CTA streaming every window through a bulk-copy ring (used when no
+// workspace for the parallel passes below is given).
 __global__ void __launch_bounds__(kSeqThreads, 1)
     sequential_clip_kernel(const float* __restrict__ g, uint64_t n, SeqClipOut out,
                            uint32_t* kernel_error, SeqCarry* carry, int resume, int finish) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t warp_val[kSeqThreads / 32];
-  __shared__ uint32_t warp_stop[kSeqThreads / 32];
-  __shared__ int32_t s_E;
-  __shared__ uint32_t s_m, s_restart, s_sum_bad, s_stop, s_total;
-  __shared__ uint32_t s_fast_total[2], s_fast_tie[2];
-  __shared__ float s_sum_bits;
-  __shared__ uint32_t s_gbad_before;
+  __shared__ SeqShared sh;
   const float* ring = reinterpret_cast<const float*>(smem);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(kSeqStages) * kSeqWindowBytes);
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   if (t == 0) {
     for (uint32_t s = 0; s < kSeqStages; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if (resume) {  // continue the sum of the slices before this one
-      s_E = carry->E;
-      s_m = carry->m;
-      s_sum_bad = carry->sum_bad;
-      s_sum_bits = carry->sum_bits;
-      s_gbad_before = carry->gbad;
-    } else {
-      s_E = -149;
-      s_m = 0u;
-      s_sum_bad = 0u;
-      s_sum_bits = 0.0f;
-      s_gbad_before = 0u;
-    }
+    seq_begin(sh, carry, resume);
   }
   __syncthreads();
   const uint64_t n_full = n / kSeqWindow;
@@ -1367,9 +1523,9 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
     // whether any term ties; if nothing ties and the sum stays in the binade
     // the whole window is one integer add.  Totals are clamped at 2^24 (any
     // such total leaves the binade, which is all that is tested).
-    if (!s_sum_bad) {
-      const int32_t E = s_E;
-      const uint32_t m = s_m;
+    if (!sh.sum_bad) {
+      const int32_t E = sh.E;
+      const uint32_t m = sh.m;
       uint32_t tsum = 0;
       bool tie_any = false;
 #pragma unroll
@@ -1381,161 +1537,259 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
       const uint32_t wsum = __reduce_add_sync(kFull, tsum < (1u << 24) ? tsum : (1u << 24));
       const uint32_t wtie = __reduce_or_sync(kFull, tie_any ? 1u : 0u);
       if (lane == 0) {
-        warp_val[warp] = wsum < (1u << 24) ? wsum : (1u << 24);
-        warp_stop[warp] = wtie;
+        sh.warp_val[warp] = wsum < (1u << 24) ? wsum : (1u << 24);
+        sh.warp_stop[warp] = wtie;
       }
       __syncthreads();
       // The window's verdict goes to slot w % 2, so the next window's write
       // never meets a thread still reading this one (no third barrier).
       const uint32_t slot = uint32_t(w & 1u);
       if (warp == 0) {
-        const uint32_t v = __reduce_add_sync(kFull, warp_val[lane]);
-        const uint32_t tw = __reduce_or_sync(kFull, warp_stop[lane]);
+        const uint32_t v = __reduce_add_sync(kFull, sh.warp_val[lane]);
+        const uint32_t tw = __reduce_or_sync(kFull, sh.warp_stop[lane]);
         if (lane == 0) {
-          s_fast_total[slot] = v;
-          s_fast_tie[slot] = tw;
+          sh.fast_total[slot] = v;
+          sh.fast_tie[slot] = tw;
         }
       }
       __syncthreads();
-      const uint32_t total = s_fast_total[slot];
-      if (s_fast_tie[slot] == 0u && uint64_t(m) + total < (1ull << 24)) {
-        if (t == 0) s_m = m + total;
+      const uint32_t total = sh.fast_total[slot];
+      if (sh.fast_tie[slot] == 0u && uint64_t(m) + total < (1ull << 24)) {
+        if (t == 0) sh.m = m + total;
         continue;  // the next window starts with a barrier
       }
-    }
-    uint32_t start = 0;  // first term of the window not yet added
-    for (;;) {           // block-uniform: every value below is read after a barrier
-      if (s_sum_bad) break;
-      const int32_t E = s_E;
-      const uint32_t m = s_m;
-      uint32_t pre[kSeqPer], run = 0, stop = kNoStop;
-#pragma unroll
-      for (uint32_t j = 0; j < kSeqPer; ++j) {
-        const uint32_t idx = 8 * t + j;
-        bool tie = false;
-        const uint32_t r = idx < start ? 0u : seq_increment(q[j], E, tie);
-        run += r;
-        pre[j] = run;
-        if (tie && stop == kNoStop) stop = idx;
-      }
-      // exclusive prefix of the thread totals over the block
-      uint32_t incl = run;
-#pragma unroll
-      for (uint32_t off = 1; off < 32; off <<= 1) {
-        const uint32_t y = __shfl_up_sync(kFull, incl, off);
-        if (lane >= off) incl += y;
-      }
-      if (lane == 31) warp_val[warp] = incl;
-      __syncthreads();
-      if (warp == 0) {
-        uint32_t v = warp_val[lane];
-#pragma unroll
-        for (uint32_t off = 1; off < 32; off <<= 1) {
-          const uint32_t y = __shfl_up_sync(kFull, v, off);
-          if (lane >= off) v += y;
-        }
-        warp_val[lane] = v;
-      }
-      __syncthreads();
-      const uint32_t excl = (incl - run) + (warp ? warp_val[warp - 1] : 0u);
-      const uint32_t total = warp_val[31];
-      // first term whose running sum would leave the binade (exact up to it)
-#pragma unroll
-      for (uint32_t j = 0; j < kSeqPer; ++j) {
-        const uint32_t idx = 8 * t + j;
-        if (idx >= start && idx < stop && uint64_t(m) + excl + pre[j] >= (1ull << 24)) stop = idx;
-      }
-      const uint32_t wmin = __reduce_min_sync(kFull, stop);
-      if (lane == 0) warp_stop[warp] = wmin;
-      __syncthreads();
-      if (warp == 0) {
-        const uint32_t v = __reduce_min_sync(kFull, warp_stop[lane]);
-        if (lane == 0) {
-          s_stop = v;
-          s_total = total;
-        }
-      }
-      __syncthreads();
-      const uint32_t first = s_stop;
-      if (first == kNoStop) {  // the whole rest of the window stays in the binade
-        if (t == 0) s_m = m + s_total;
-        __syncthreads();
-        break;
-      }
-      if (first >= 8 * t && first < 8 * t + kSeqPer) {  // the owner of the stopping term
-        const uint32_t j0 = first - 8 * t;
-        uint32_t before = excl;
-        float qj = 0.0f;
-#pragma unroll
-        for (uint32_t j = 0; j < kSeqPer; ++j) {  // no dynamic register indexing
-          if (j + 1 == j0) before += pre[j];
-          if (j == j0) qj = q[j];
-        }
-        const float sum = __fadd_rn(seq_compose(E, m + before), qj);
-        if (!finite_f32(sum)) {
-          s_sum_bad = 1u;
-          s_sum_bits = sum;
-        } else {
-          int32_t E2;
-          uint32_t m2;
-          seq_decompose(sum, E2, m2);
-          s_E = E2;
-          s_m = m2;
-        }
-        s_restart = first + 1;
-      }
-      __syncthreads();
-      start = s_restart;
-      if (start >= kSeqWindow) break;
+      seq_window_exact(sh, q);
     }
   }
   // After a failed wait thread 0 waits (bounded) for its copies in flight.
   if (!ok && t == 0)
     for (uint64_t u = issued > kSeqStages ? issued - kSeqStages : 0; u < issued; ++u)
       mbar_wait(&full[u % kSeqStages], uint32_t(u / kSeqStages) & 1u);
-  const int any_bad = __syncthreads_or(gbad ? 1 : 0) || s_gbad_before;
-  if (t != 0) return;
-  if (!ok) {
-    atomicOr(kernel_error, 1u);
-    return;
+  const bool any_bad = __syncthreads_or(gbad ? 1 : 0) || sh.gbad_before;
+  if (t == 0) seq_store(sh, any_bad, ok, out, kernel_error, carry, finish);
+}
+
+// ---- the same sum with every SM: candidate binades, then one chain ----------------
+// While the sum stays in a binade, a whole window adds an integer number of
+// ulps that depends only on that binade.  So windows are summarised in
+// parallel first -- for each, its total increment and tie flag under the
+// kSeqCand binades the running sum can plausibly be in there (around the
+// binade of the window's exact f64 prefix sum, since the in-order f32 sum
+// drifts from it by well under a factor of 4 in practice) -- and one CTA
+// then chains the windows in order through those summaries, adding the exact
+// window procedure above only where the sum's binade is not among the
+// candidates, a term ties, or the window's total leaves the binade.  Which
+// binades are candidates affects only how many windows take the exact path,
+// never the result.
+constexpr int kSeqCand = 4;
+constexpr uint32_t kSeqPassThreads = 256;
+constexpr uint32_t kSeqChainBatch = 1024;  // window summaries per shared-memory batch
+
+struct SeqWorkspace {  // per window: exact sum, candidate base, totals, flags
+  double* sums;
+  int32_t* base;
+  uint32_t* total;  // kSeqCand per window, clamped at 2^24
+  uint8_t* flags;   // bit c: candidate c ties; bit 7: a non-finite gradient
+};
+
+__device__ __forceinline__ int32_t seq_binade(float s) {
+  const uint32_t exp = (__float_as_uint(s) >> 23) & 0xffu;
+  return exp == 0u ? -149 : int32_t(exp) - 150;
+}
+
+__global__ void __launch_bounds__(kSeqPassThreads)
+    seqclip_sums_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
+                        SeqWorkspace ws) {
+  __shared__ double wsum[kSeqPassThreads / 32];
+  __shared__ uint32_t wbad[kSeqPassThreads / 32];
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  for (uint64_t w = blockIdx.x; w < n_windows; w += gridDim.x) {
+    double acc = 0.0;
+    bool bad = false;
+    for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads; ++k) {
+      const uint64_t i = w * kSeqWindow + uint64_t(k) * kSeqPassThreads + t;
+      const float x = i < n ? g[i] : 0.0f;
+      bad |= !finite_f32(x);
+      acc += double(__fmul_rn(x, x));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) acc += __shfl_down_sync(kFull, acc, off);
+    const uint32_t b = __reduce_or_sync(kFull, bad ? 1u : 0u);
+    if (lane == 0) {
+      wsum[warp] = acc;
+      wbad[warp] = b;
+    }
+    __syncthreads();
+    if (t == 0) {
+      double s = 0.0;
+      uint32_t bb = 0;
+      for (uint32_t i = 0; i < kSeqPassThreads / 32; ++i) {
+        s += wsum[i];
+        bb |= wbad[i];
+      }
+      ws.sums[w] = s;
+      ws.flags[w] = bb ? 0x80u : 0u;
+    }
+    __syncthreads();
   }
-  if (!finish) {  // hand the running sum to the launch for the next slice
-    carry->E = s_E;
-    carry->m = s_m;
-    carry->sum_bad = s_sum_bad;
-    carry->sum_bits = s_sum_bits;
-    carry->gbad = any_bad ? 1u : 0u;
-    return;
+}
+
+// Exclusive prefix of the window sums (continuing the previous slice's) and
+// each window's first candidate binade.  One CTA.
+__global__ void __launch_bounds__(kSeqThreads)
+    seqclip_prefix_kernel(uint64_t n_windows, SeqWorkspace ws, SeqCarry* carry, int resume,
+                          int keep) {
+  __shared__ double part[kSeqThreads];
+  __shared__ double s_start;
+  const uint32_t t = threadIdx.x;
+  const uint64_t per = (n_windows + kSeqThreads - 1) / kSeqThreads;
+  const uint64_t lo = uint64_t(t) * per;
+  const uint64_t hi = lo + per < n_windows ? lo + per : n_windows;
+  double mine = 0.0;
+  for (uint64_t w = lo; w < hi; ++w) mine += ws.sums[w];
+  part[t] = mine;
+  if (t == 0) s_start = resume ? carry->prefix : 0.0;
+  __syncthreads();
+  if (t == 0) {  // in order over the 1,024 thread sums
+    double run = s_start;
+    for (uint32_t i = 0; i < kSeqThreads; ++i) {
+      const double v = part[i];
+      part[i] = run;
+      run += v;
+    }
+    if (keep) carry->prefix = run;
   }
-  const float sum = s_sum_bad ? s_sum_bits : seq_compose(s_E, s_m);
-  int32_t status = kStatusOk;
-  float clip = 1.0f;
-  if (any_bad) {
-    status = kStatusGradientNonfinite;
-  } else if (!finite_f32(sum)) {
-    status = kStatusNormNonfinite;
-  } else if (sum != 0.0f) {
-    const float c = __fdiv_rn(1.0f, __fsqrt_rn(sum));
-    clip = c < 1.0f ? c : 1.0f;
+  __syncthreads();
+  double p = part[t];
+  for (uint64_t w = lo; w < hi; ++w) {
+    ws.base[w] = seq_binade(float(p)) - (kSeqCand / 2);
+    p += ws.sums[w];
   }
-  if (out.st) {
-    DeviceStepState* st = out.st;
-    st->sum_squares = double(sum);
-    st->grad_norm = double(__fsqrt_rn(sum));
-    st->clip_scale = clip;
-    st->clip_apply = 1.0f;  // the gradients arrive clipped
-    st->loss_scale_used = 1.0f;
-    st->next_loss_scale = 1.0f;
-    st->skipped = status == kStatusOk ? 0u : 1u;
-    st->nonfinite = status == kStatusOk ? 0u : 1u;
-    st->result_nonfinite = 0u;
-    st->rejected = 0u;
-    st->status = status;
-  } else {
-    *out.sum = sum;
-    *out.clip = clip;
-    *out.status = status;
+}
+
+__global__ void __launch_bounds__(kSeqPassThreads)
+    seqclip_candidates_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
+                              SeqWorkspace ws) {
+  __shared__ uint32_t wtot[kSeqCand][kSeqPassThreads / 32];
+  __shared__ uint32_t wtie[kSeqPassThreads / 32];
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  for (uint64_t w = blockIdx.x; w < n_windows; w += gridDim.x) {
+    const int32_t E0 = ws.base[w];
+    uint32_t tot[kSeqCand] = {};
+    uint32_t ties = 0;
+    for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads; ++k) {
+      const uint64_t i = w * kSeqWindow + uint64_t(k) * kSeqPassThreads + t;
+      const float x = i < n ? g[i] : 0.0f;
+      const float q = __fmul_rn(x, x);
+#pragma unroll
+      for (int c = 0; c < kSeqCand; ++c) {
+        bool tie;
+        tot[c] += seq_increment(q, E0 + c, tie);  // <= 32 * 2^25: no wrap
+        ties |= tie ? (1u << c) : 0u;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kSeqCand; ++c) {
+      const uint32_t v = __reduce_add_sync(kFull, tot[c] < (1u << 24) ? tot[c] : (1u << 24));
+      if (lane == 0) wtot[c][warp] = v < (1u << 24) ? v : (1u << 24);
+    }
+    const uint32_t tw = __reduce_or_sync(kFull, ties);
+    if (lane == 0) wtie[warp] = tw;
+    __syncthreads();
+    if (t < kSeqCand) {
+      uint32_t v = 0;
+      for (uint32_t i = 0; i < kSeqPassThreads / 32; ++i) v += wtot[t][i];
+      ws.total[w * kSeqCand + t] = v < (1u << 24) ? v : (1u << 24);
+    }
+    if (t == 0) {
+      uint32_t tb = 0;
+      for (uint32_t i = 0; i < kSeqPassThreads / 32; ++i) tb |= wtie[i];
+      ws.flags[w] = uint8_t(ws.flags[w] | tb);
+    }
+    __syncthreads();
   }
+}
+
+// One CTA chains the window summaries in order; thread 0 walks a batch of
+// them from shared memory, and at a window the summaries cannot decide all
+// threads add that window exactly.
+__global__ void __launch_bounds__(kSeqThreads, 1)
+    seqclip_chain_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
+                         SeqWorkspace ws, SeqClipOut out, uint32_t* kernel_error,
+                         SeqCarry* carry, int resume, int finish) {
+  __shared__ SeqShared sh;
+  __shared__ int32_t b_base[kSeqChainBatch];
+  __shared__ uint8_t b_flags[kSeqChainBatch];
+  __shared__ uint32_t b_total[kSeqChainBatch * kSeqCand];
+  __shared__ uint32_t s_next, s_miss, s_gbad;
+  const uint32_t t = threadIdx.x;
+  if (t == 0) {
+    seq_begin(sh, carry, resume);
+    s_gbad = 0u;
+  }
+  bool gbad = false;
+  for (uint64_t b0 = 0; b0 < n_windows; b0 += kSeqChainBatch) {
+    const uint32_t nb = uint32_t(n_windows - b0 < kSeqChainBatch ? n_windows - b0
+                                                                  : kSeqChainBatch);
+    __syncthreads();  // the previous batch is no longer read
+    for (uint32_t i = t; i < nb; i += kSeqThreads) {
+      b_base[i] = ws.base[b0 + i];
+      b_flags[i] = ws.flags[b0 + i];
+    }
+    for (uint32_t i = t; i < nb * kSeqCand; i += kSeqThreads)
+      b_total[i] = ws.total[b0 * kSeqCand + i];
+    if (t == 0) s_next = 0u;
+    __syncthreads();
+    for (;;) {  // block-uniform: s_next and s_miss are read after a barrier
+      if (t == 0) {
+        uint32_t k = s_next;
+        uint32_t gb = 0u;
+        uint32_t miss = 0u;
+        if (sh.sum_bad) {  // the sum is no longer finite: only the flags matter
+          for (; k < nb; ++k) gb |= b_flags[k];
+        } else {
+          const int32_t E = sh.E;
+          uint32_t m = sh.m;
+          for (; k < nb; ++k) {
+            const uint32_t f = b_flags[k];
+            gb |= f;
+            const int32_t c = E - b_base[k];
+            if (c < 0 || c >= kSeqCand || ((f >> c) & 1u)) {
+              miss = 1u;
+              break;
+            }
+            const uint32_t tot = b_total[k * kSeqCand + c];
+            if (uint64_t(m) + tot >= (1ull << 24)) {
+              miss = 1u;
+              break;
+            }
+            m += tot;
+          }
+          sh.m = m;
+        }
+        s_gbad |= gb & 0x80u;
+        s_next = k;
+        s_miss = miss;
+      }
+      __syncthreads();
+      if (!s_miss) break;
+      // The window the summaries could not add: every thread takes its 8 terms.
+      const uint64_t w = b0 + s_next;
+      float q[kSeqPer];
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        const uint64_t i = w * kSeqWindow + 8 * t + j;
+        const float x = i < n ? g[i] : 0.0f;
+        gbad |= !finite_f32(x);
+        q[j] = __fmul_rn(x, x);
+      }
+      seq_window_exact(sh, q);
+      if (t == 0) s_next += 1u;
+      __syncthreads();
+    }
+  }
+  const bool any_bad = __syncthreads_or(gbad ? 1 : 0) || s_gbad || sh.gbad_before;
+  if (t == 0) seq_store(sh, any_bad, true, out, kernel_error, carry, finish);
 }
 
 // ---- state initialisation / validation ----------------------------------------
@@ -2370,15 +2624,44 @@ cudaError_t launch_init_from_master(float* master, float* moment, float* varianc
 }
 
 cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, void* workspace, size_t workspace_bytes) {
   SeqClipOut out{st, nullptr, nullptr, nullptr};
-  return launch_sequential_clip(g, n, out, &st->kernel_error, stream);
+  return launch_sequential_clip(g, n, out, &st->kernel_error, stream, nullptr, false, true,
+                                workspace, workspace_bytes);
+}
+
+size_t seq_clip_workspace_bytes(uint64_t n) {
+  const uint64_t nw = (n + kSeqWindow - 1) / kSeqWindow;
+  const uint64_t bytes = nw * (sizeof(double) + sizeof(int32_t) + kSeqCand * sizeof(uint32_t) + 1);
+  return size_t((bytes + 15) & ~uint64_t(15));
 }
 
 cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
                                    uint32_t* kernel_error, cudaStream_t stream, SeqCarry* carry,
-                                   bool resume, bool finish) {
+                                   bool resume, bool finish, void* workspace,
+                                   size_t workspace_bytes) {
   if ((resume || !finish) && carry == nullptr) return cudaErrorInvalidValue;
+  const uint64_t n_windows = (n + kSeqWindow - 1) / kSeqWindow;
+  if (workspace != nullptr && n_windows > 0) {
+    if (workspace_bytes < seq_clip_workspace_bytes(n) ||
+        reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+      return cudaErrorInvalidValue;
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    SeqWorkspace ws;
+    ws.sums = reinterpret_cast<double*>(base);
+    ws.base = reinterpret_cast<int32_t*>(base + n_windows * sizeof(double));
+    ws.total = reinterpret_cast<uint32_t*>(base + n_windows * (sizeof(double) + sizeof(int32_t)));
+    ws.flags = base + n_windows * (sizeof(double) + sizeof(int32_t) + kSeqCand * sizeof(uint32_t));
+    const uint64_t cap = uint64_t(current_sms()) * 8;
+    const unsigned grid = unsigned(n_windows < cap ? n_windows : cap);
+    seqclip_sums_kernel<<<grid, kSeqPassThreads, 0, stream>>>(g, n, n_windows, ws);
+    seqclip_prefix_kernel<<<1, kSeqThreads, 0, stream>>>(n_windows, ws, carry, resume ? 1 : 0,
+                                                         !finish ? 1 : 0);
+    seqclip_candidates_kernel<<<grid, kSeqPassThreads, 0, stream>>>(g, n, n_windows, ws);
+    seqclip_chain_kernel<<<1, kSeqThreads, 0, stream>>>(g, n, n_windows, ws, out, kernel_error,
+                                                        carry, resume ? 1 : 0, finish ? 1 : 0);
+    return cudaGetLastError();
+  }
   const int bytes = int(kSeqStages * kSeqWindowBytes + kBarrierBytes);
   cudaError_t e = cudaFuncSetAttribute(sequential_clip_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);

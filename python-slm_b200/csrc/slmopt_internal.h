@@ -201,7 +201,8 @@ cudaError_t launch_export_f32(const uint16_t* w16, float* dst, uint64_t n, cudaS
 // sum of squares over g[0..n) (16-byte aligned), then min(1/sqrt(sum), 1);
 // fills st as the norm pass would for a static scale of 1 without clipping.
 cudaError_t launch_reference_clip(const float* g, uint64_t n, DeviceStepState* st,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, void* workspace = nullptr,
+                                  size_t workspace_bytes = 0);
 // The same sequential clip scale with its result sent elsewhere: into the step
 // record (st != NULL) or into the three caller-provided device words.
 struct SeqClipOut {
@@ -218,15 +219,21 @@ struct SeqCarry {
   uint32_t sum_bad;   // the sum became non-finite (sum_bits holds it)
   float sum_bits;
   uint32_t gbad;      // a non-finite gradient was seen
-  uint32_t reserved[3];
+  uint32_t reserved;
+  double prefix;      // exact (f64) sum of the slices before, for the parallel form
 };
 constexpr uint64_t kSeqSliceAlign = 8192;  // terms per window of the sequential sum
 // resume: start from *carry (else from zero); finish: write the result to
-// `out` (else save the running state to *carry).
+// `out` (else save the running state to *carry).  With a workspace of
+// seq_clip_workspace_bytes(n) bytes (16-byte aligned) the windows are
+// summarised by every SM first and one CTA chains the summaries; without one
+// a single CTA streams all n terms.  Both give the same bits.
+size_t seq_clip_workspace_bytes(uint64_t n);
 cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut& out,
                                    uint32_t* kernel_error, cudaStream_t stream,
                                    SeqCarry* carry = nullptr, bool resume = false,
-                                   bool finish = true);
+                                   bool finish = true, void* workspace = nullptr,
+                                   size_t workspace_bytes = 0);
 cudaError_t launch_init_from_master(float* master, float* moment, float* variance, uint16_t* w16,
                                     uint64_t n, cudaStream_t stream);
 cudaError_t launch_validate_state(const float* master, const float* moment,

@@ -173,6 +173,8 @@ SIGNATURES = [
     ("slm_opt_gradient_buffer", _I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_U64)]),
     ("slm_grad_norm_noalloc", _I, [_P, _I, _U64, _F, _F, _P, _P]),
     ("slm_gradient_clip_scale", _I, [_P, _U64, _P, _P]),
+    ("slm_gradient_clip_workspace_bytes", _U64, [_U64]),
+    ("slm_gradient_clip_scale_ws", _I, [_P, _U64, _P, _U64, _P, _P]),
     ("slm_opt_set_loss_scale", _I, [_P, _F, _U32]),
     ("slm_opt_get_loss_scale", _I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_U32)]),
     ("slm_canonical_learning_rate", _I, [_U64, ctypes.POINTER(_F)]),

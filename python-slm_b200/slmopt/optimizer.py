@@ -324,19 +324,29 @@ class B200Adamw:
         return buf.value.decode() if with_sha else None
 
 
-def gradient_clip_scale(gradients, stream=None) -> tuple[int, float, float]:
+def gradient_clip_scale(gradients, stream=None, parallel: bool = True) -> tuple[int, float, float]:
     """The reference's gradient_clip_scale (src/model/oracle.rs:486-507) of a
     contiguous f32 CUDA tensor, bit for bit, on the device:
-    (status, sequential f32 sum of squares, clip scale).  Waits for the
-    result."""
+    (status, sequential f32 sum of squares, clip scale).  parallel=True
+    summarises the windows on every SM (slm_gradient_clip_scale_ws, with a
+    workspace allocated here); False streams them through one CTA
+    (slm_gradient_clip_scale).  Waits for the result."""
     import torch
 
     if not (gradients.is_cuda and gradients.dtype == torch.float32 and gradients.is_contiguous()):
         raise ValueError("gradients must be a contiguous f32 CUDA tensor")
     lib = _lib.load()
+    n = gradients.numel()
     out = torch.zeros(ctypes.sizeof(_lib.ClipResult), dtype=torch.uint8, device=gradients.device)
-    _lib.check(lib.slm_gradient_clip_scale(gradients.data_ptr(), gradients.numel(), out.data_ptr(),
-                                           _stream_handle(stream)))
+    if parallel:
+        ws_bytes = int(lib.slm_gradient_clip_workspace_bytes(n))
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=gradients.device)
+        _lib.check(lib.slm_gradient_clip_scale_ws(gradients.data_ptr(), n, ws.data_ptr(),
+                                                  ws_bytes, out.data_ptr(),
+                                                  _stream_handle(stream)))
+    else:
+        _lib.check(lib.slm_gradient_clip_scale(gradients.data_ptr(), n, out.data_ptr(),
+                                               _stream_handle(stream)))
     res = _lib.ClipResult.from_buffer_copy(out.cpu().numpy().tobytes())
     if res.kernel_error:
         raise _lib.SlmError(_lib.SLM_ERR_INTERNAL, "the clip scale kernel's copy pipeline stalled")

@@ -712,20 +712,31 @@ def _clip_cases():
     nan = rng.standard_normal(50_000).astype(np.float32)
     nan[9_000] = np.nan
     cases["nan"] = nan
+    # the sum crosses a binade every few hundred terms, inside windows
+    cases["crossings"] = np.geomspace(1e-6, 1e3, 400_000).astype(np.float32)
+    # large squares early, then small ones: the running f32 sum stops moving
+    # for long stretches while the exact prefix keeps growing
+    stall = np.full(2_000_000, np.float32(np.sqrt(0.9) * 2.0**-12), np.float32)
+    stall[:3] = 1.0
+    cases["stalled"] = stall
+    late = (rng.standard_normal(100_000) * 1e18).astype(np.float32)
+    late[77_777] = np.nan  # after the sum overflowed: still a non-finite gradient
+    cases["overflow_then_nan"] = late
     return cases
 
 
 CLIP_CASES = _clip_cases()
 
 
+@pytest.mark.parametrize("parallel", [True, False], ids=["all_sms", "one_cta"])
 @pytest.mark.parametrize("name", sorted(CLIP_CASES))
-def test_gradient_clip_scale_is_the_reference_sequential_sum(torch, name):
+def test_gradient_clip_scale_is_the_reference_sequential_sum(torch, name, parallel):
     from slmopt.optimizer import gradient_clip_scale
 
     g = CLIP_CASES[name]
     dev = torch.from_numpy(g).cuda() if g.size else torch.zeros(0, dtype=torch.float32,
                                                                  device="cuda")
-    status, got_sum, got_clip = gradient_clip_scale(dev)
+    status, got_sum, got_clip = gradient_clip_scale(dev, parallel=parallel)
     want_status, want_clip = oracle.gradient_clip_scale(g)
     sum_status, want_sum = oracle.reference_sum_squares(g)
     assert status == want_status, (status, want_status)
@@ -736,7 +747,8 @@ def test_gradient_clip_scale_is_the_reference_sequential_sum(torch, name):
         assert sum_status == 0 and not np.isfinite(want_sum) and not np.isfinite(got_sum)
 
 
-def test_gradient_clip_scale_at_production_width(torch):
+@pytest.mark.parametrize("parallel", [True, False], ids=["all_sms", "one_cta"])
+def test_gradient_clip_scale_at_production_width(torch, parallel):
     # the reference's 135,285,504-element probe shape: a clipped gradient whose
     # sequential f32 sum drifts ~35 % below the exact one
     from slmopt.optimizer import gradient_clip_scale
@@ -744,7 +756,7 @@ def test_gradient_clip_scale_at_production_width(torch):
     n = 135_285_504
     g = synth.grads_f32(n, 1)
     g *= np.float32(0.9 / float(np.sqrt(np.sum(g.astype(np.float64) ** 2))))
-    status, got_sum, got_clip = gradient_clip_scale(torch.from_numpy(g).cuda())
+    status, got_sum, got_clip = gradient_clip_scale(torch.from_numpy(g).cuda(), parallel=parallel)
     st, want_sum = oracle.reference_sum_squares(g)
     assert status == 0 and st == 0
     assert np.float32(got_sum).view(np.uint32) == np.float32(want_sum).view(np.uint32)

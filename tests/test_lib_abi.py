@@ -139,6 +139,7 @@ def test_every_handle_entry_point_rejects_null_arguments():
         "slm_grad_accumulate": (None, None, 1, 0, 0, None),
         "slm_grad_norm_noalloc": (None, 1, 10, one, one, None, None),
         "slm_gradient_clip_scale": (None, 10, None, None),
+        "slm_gradient_clip_scale_ws": (None, 10, None, 0, None, None),
     }
     for name, args in calls.items():
         assert getattr(lib, name)(*args) == _lib.SLM_ERR_INVALID_ARGUMENT, name
@@ -162,3 +163,23 @@ def test_noalloc_norm_rejects_misaligned_pointers_before_touching_a_device():
         st = lib.slm_grad_norm_noalloc(grads, dtype, 16, one, one, out, None)
         assert st == _lib.SLM_ERR_INVALID_ARGUMENT, (grads, dtype, out)
         assert "align" in lib.slm_last_error_message().decode()
+
+
+def test_clip_workspace_size_and_validation_without_a_device():
+    # 29 bytes per 8,192-gradient window (f64 sum, i32 base binade, four u32
+    # totals, one flag byte), rounded up to 16; a workspace that is smaller or
+    # misaligned is refused before any launch.
+    lib = _lib.load()
+    assert lib.slm_gradient_clip_workspace_bytes(0) == 0
+    assert lib.slm_gradient_clip_workspace_bytes(1) == 32
+    assert lib.slm_gradient_clip_workspace_bytes(8192) == 32
+    assert lib.slm_gradient_clip_workspace_bytes(8193) == 64
+    assert lib.slm_gradient_clip_workspace_bytes(135_285_504) == 478_944  # 16,515 windows
+    need = lib.slm_gradient_clip_workspace_bytes(10 * 8192)
+    grads, ws, out = 0x10000, 0x20000, 0x30000
+    st = lib.slm_gradient_clip_scale_ws(grads, 10 * 8192, ws, need - 16, out, None)
+    assert st == _lib.SLM_ERR_INVALID_ARGUMENT
+    assert "workspace" in lib.slm_last_error_message().decode()
+    st = lib.slm_gradient_clip_scale_ws(grads, 10 * 8192, ws + 8, need, out, None)
+    assert st == _lib.SLM_ERR_INVALID_ARGUMENT
+    assert "align" in lib.slm_last_error_message().decode()

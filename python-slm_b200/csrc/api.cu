@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <memory>
 #include <new>
 #include <set>
@@ -288,8 +289,14 @@ int stage_pageable(slm_opt_handle* h, void* dst, const void* src, size_t bytes,
   if (st) return st;
 
   const size_t n_slices = (bytes + Ring::kSlotBytes - 1) / Ring::kSlotBytes;
+  // Host threads filling the ring: half the host's hardware threads, at most
+  // 8, unless SLM_STAGING_THREADS (1..64) says otherwise.
   const unsigned hw = std::thread::hardware_concurrency();
-  const size_t T = std::min<size_t>(8, std::max<size_t>(1, hw / 2));
+  size_t T = std::min<size_t>(8, std::max<size_t>(1, hw / 2));
+  if (const char* env = std::getenv("SLM_STAGING_THREADS")) {
+    const long v = std::strtol(env, nullptr, 10);
+    if (v >= 1 && v <= 64) T = size_t(v);
+  }
   std::unique_ptr<std::atomic<size_t>[]> parts(new std::atomic<size_t>[n_slices]);
   for (size_t c = 0; c < n_slices; ++c) parts[c].store(0);
   std::atomic<size_t> go{0};  // slices whose slot is free to be filled

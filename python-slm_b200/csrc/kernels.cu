@@ -1585,16 +1585,46 @@ constexpr int kSeqCand = 4;
 constexpr uint32_t kSeqPassThreads = 256;
 constexpr uint32_t kSeqChainBatch = 1024;  // window summaries per shared-memory batch
 
-struct SeqWorkspace {  // per window: exact sum, candidate base, totals, flags
+struct SeqWorkspace {  // per window: totals, exact sum, candidate base, flags
+  uint32_t* total;  // kSeqCand per window (16 bytes), clamped at 2^24
   double* sums;
   int32_t* base;
-  uint32_t* total;  // kSeqCand per window, clamped at 2^24
   uint8_t* flags;   // bit c: candidate c ties; bit 7: a non-finite gradient
 };
+static_assert(kSeqCand == 4, "a window's candidate totals are one 16-byte record");
+
+__device__ __forceinline__ uint32_t seq_pick(const uint4& v, int32_t c) {
+  return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
+}
 
 __device__ __forceinline__ int32_t seq_binade(float s) {
   const uint32_t exp = (__float_as_uint(s) >> 23) & 0xffu;
   return exp == 0u ? -149 : int32_t(exp) - 150;
+}
+
+// Thread t's 32 terms of window w, as 8 coalesced 16-byte loads for a whole
+// window (the passes below need no particular order within a window); the
+// ragged last window element by element, zeros past n.
+__device__ __forceinline__ void seq_pass_load(const float* __restrict__ g, uint64_t n,
+                                              uint64_t w, float (&x)[kSeqWindow / kSeqPassThreads]) {
+  const uint32_t t = threadIdx.x;
+  if ((w + 1) * kSeqWindow <= n) {
+    const float4* v = reinterpret_cast<const float4*>(g + w * kSeqWindow);
+#pragma unroll
+    for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads / 4; ++k) {
+      const float4 a = __ldg(v + t + kSeqPassThreads * k);
+      x[4 * k] = a.x;
+      x[4 * k + 1] = a.y;
+      x[4 * k + 2] = a.z;
+      x[4 * k + 3] = a.w;
+    }
+  } else {
+#pragma unroll
+    for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads; ++k) {
+      const uint64_t i = w * kSeqWindow + uint64_t(t + kSeqPassThreads * (k / 4)) * 4 + k % 4;
+      x[k] = i < n ? g[i] : 0.0f;
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kSeqPassThreads)
@@ -1604,13 +1634,14 @@ __global__ void __launch_bounds__(kSeqPassThreads)
   __shared__ uint32_t wbad[kSeqPassThreads / 32];
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   for (uint64_t w = blockIdx.x; w < n_windows; w += gridDim.x) {
+    float x[kSeqWindow / kSeqPassThreads];
+    seq_pass_load(g, n, w, x);
     double acc = 0.0;
     bool bad = false;
+#pragma unroll
     for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads; ++k) {
-      const uint64_t i = w * kSeqWindow + uint64_t(k) * kSeqPassThreads + t;
-      const float x = i < n ? g[i] : 0.0f;
-      bad |= !finite_f32(x);
-      acc += double(__fmul_rn(x, x));
+      bad |= !finite_f32(x[k]);
+      acc += double(__fmul_rn(x[k], x[k]));
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) acc += __shfl_down_sync(kFull, acc, off);
@@ -1635,38 +1666,85 @@ __global__ void __launch_bounds__(kSeqPassThreads)
 }
 
 // Exclusive prefix of the window sums (continuing the previous slice's) and
-// each window's first candidate binade.  One CTA.
+// each window's first candidate binade.  One CTA: warp w owns a run of
+// `steps` x 32 consecutive windows, lane l the windows l, l + 32, ... of it
+// (coalesced loads, all issued before they are added); the warps' totals are
+// scanned across the block, then every warp scans its run 32 windows at a
+// time.  Any order of the f64 additions will do: the prefix only chooses
+// candidates.
 __global__ void __launch_bounds__(kSeqThreads)
     seqclip_prefix_kernel(uint64_t n_windows, SeqWorkspace ws, SeqCarry* carry, int resume,
                           int keep) {
-  __shared__ double part[kSeqThreads];
+  __shared__ double warp_tot[kSeqThreads / 32];
   __shared__ double s_start;
-  const uint32_t t = threadIdx.x;
-  const uint64_t per = (n_windows + kSeqThreads - 1) / kSeqThreads;
-  const uint64_t lo = uint64_t(t) * per;
-  const uint64_t hi = lo + per < n_windows ? lo + per : n_windows;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint64_t steps = (n_windows + kSeqThreads - 1) / kSeqThreads;
+  const uint64_t w_lo = uint64_t(warp) * steps * 32;
+  auto load8 = [&](uint64_t j0, double (&v)[8]) {
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      const uint64_t idx = w_lo + (j0 + j) * 32 + lane;
+      v[j] = j0 + j < steps && idx < n_windows ? ws.sums[idx] : 0.0;
+    }
+  };
   double mine = 0.0;
-  for (uint64_t w = lo; w < hi; ++w) mine += ws.sums[w];
-  part[t] = mine;
+  for (uint64_t j0 = 0; j0 < steps; j0 += 8) {
+    double v[8];
+    load8(j0, v);
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) mine += v[j];
+  }
+#pragma unroll
+  for (uint32_t off = 16; off >= 1; off >>= 1) mine += __shfl_xor_sync(kFull, mine, off);
+  if (lane == 0) warp_tot[warp] = mine;
   if (t == 0) s_start = resume ? carry->prefix : 0.0;
   __syncthreads();
-  if (t == 0) {  // in order over the 1,024 thread sums
-    double run = s_start;
-    for (uint32_t i = 0; i < kSeqThreads; ++i) {
-      const double v = part[i];
-      part[i] = run;
-      run += v;
+  if (warp == 0) {
+    double v = warp_tot[lane];
+#pragma unroll
+    for (uint32_t off = 1; off < 32; off <<= 1) {
+      const double y = __shfl_up_sync(kFull, v, off);
+      if (lane >= off) v += y;
     }
-    if (keep) carry->prefix = run;
+    warp_tot[lane] = v;  // inclusive
   }
   __syncthreads();
-  double p = part[t];
-  for (uint64_t w = lo; w < hi; ++w) {
-    ws.base[w] = seq_binade(float(p)) - (kSeqCand / 2);
-    p += ws.sums[w];
+  double run = s_start + (warp ? warp_tot[warp - 1] : 0.0);
+  for (uint64_t j0 = 0; j0 < steps; j0 += 8) {
+    double v[8];
+    load8(j0, v);
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) {
+      double incl = v[j];
+#pragma unroll
+      for (uint32_t off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(kFull, incl, off);
+        if (lane >= off) incl += y;
+      }
+      const uint64_t idx = w_lo + (j0 + j) * 32 + lane;
+      if (j0 + j < steps && idx < n_windows)
+        ws.base[idx] = seq_binade(float(run + (incl - v[j]))) - (kSeqCand / 2);
+      run += __shfl_sync(kFull, incl, 31);
+    }
   }
+  if (keep && t == 0) carry->prefix = s_start + warp_tot[kSeqThreads / 32 - 1];
 }
 
+// 2^k as an f32, k in [-149, 127].
+__device__ __forceinline__ float seq_pow2(int32_t k) {
+  return k >= -126 ? __uint_as_float(uint32_t(k + 127) << 23) : __uint_as_float(1u << (k + 149));
+}
+
+// Per window and candidate binade E = base + c: the window's total increment
+// sum(round(q / 2^E)) and whether some q / 2^E has a fractional part of
+// exactly one half (a tie, which the chain resolves term by term).  In f32:
+// y = q / 2^E is exact (a power-of-two scaling; an overflow means y >= 2^24
+// anyway, an underflow means y < 2^-126, an increment of 0 that cannot tie),
+// rintf(y) is the increment wherever there is no tie, y - rintf(y) is exact
+// and is +-0.5 exactly at a tie, and an f32 running total of non-negative
+// integers is exact below 2^24 and stays >= 2^24 once the exact total gets
+// there -- all the chain needs (totals are clamped at 2^24).  An infinite or
+// NaN term gives a total of 2^24 (the chain then adds that window exactly).
 __global__ void __launch_bounds__(kSeqPassThreads)
     seqclip_candidates_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
                               SeqWorkspace ws) {
@@ -1674,24 +1752,31 @@ __global__ void __launch_bounds__(kSeqPassThreads)
   __shared__ uint32_t wtie[kSeqPassThreads / 32];
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   for (uint64_t w = blockIdx.x; w < n_windows; w += gridDim.x) {
-    const int32_t E0 = ws.base[w];
-    uint32_t tot[kSeqCand] = {};
-    uint32_t ties = 0;
-    for (uint32_t k = 0; k < kSeqWindow / kSeqPassThreads; ++k) {
-      const uint64_t i = w * kSeqWindow + uint64_t(k) * kSeqPassThreads + t;
-      const float x = i < n ? g[i] : 0.0f;
-      const float q = __fmul_rn(x, x);
+    float x[kSeqWindow / kSeqPassThreads];
+    seq_pass_load(g, n, w, x);
+    const int32_t k = -ws.base[w];  // in [-104, 151]: base >= -151
+    const bool split = k > 127;
+    const float s0 = seq_pow2(split ? k - 64 : (k < -149 ? -149 : k));
+    const float s1 = split ? seq_pow2(64) : 1.0f;
+    float tot[kSeqCand] = {}, dev[kSeqCand] = {};
+#pragma unroll
+    for (uint32_t j = 0; j < kSeqWindow / kSeqPassThreads; ++j) {
+      float y = __fmul_rn(__fmul_rn(__fmul_rn(x[j], x[j]), s0), s1);
 #pragma unroll
       for (int c = 0; c < kSeqCand; ++c) {
-        bool tie;
-        tot[c] += seq_increment(q, E0 + c, tie);  // <= 32 * 2^25: no wrap
-        ties |= tie ? (1u << c) : 0u;
+        const float r = rintf(y);
+        tot[c] = __fadd_rn(tot[c], r);
+        dev[c] = fmaxf(dev[c], fabsf(__fsub_rn(y, r)));
+        y = __fmul_rn(y, 0.5f);
       }
     }
+    uint32_t ties = 0;
 #pragma unroll
     for (int c = 0; c < kSeqCand; ++c) {
-      const uint32_t v = __reduce_add_sync(kFull, tot[c] < (1u << 24) ? tot[c] : (1u << 24));
-      if (lane == 0) wtot[c][warp] = v < (1u << 24) ? v : (1u << 24);
+      const uint32_t v = tot[c] < 16777216.0f ? uint32_t(tot[c]) : (1u << 24);  // NaN too
+      const uint32_t sum = __reduce_add_sync(kFull, v);  // 32 x 2^24: no wrap
+      if (lane == 0) wtot[c][warp] = sum < (1u << 24) ? sum : (1u << 24);
+      ties |= dev[c] == 0.5f ? (1u << c) : 0u;
     }
     const uint32_t tw = __reduce_or_sync(kFull, ties);
     if (lane == 0) wtie[warp] = tw;
@@ -1710,85 +1795,164 @@ __global__ void __launch_bounds__(kSeqPassThreads)
   }
 }
 
-// One CTA chains the window summaries in order; thread 0 walks a batch of
-// them from shared memory, and at a window the summaries cannot decide all
-// threads add that window exactly.
+// One CTA chains the window summaries in order.  A batch of 1,024 windows is
+// read into shared memory and summarised once more per group of 32 windows
+// (warp j: group j): for each of the 4 binades from the group's first base,
+// the group's total and whether every window of the group has that binade
+// among its candidates without a tie.  Warp 0 then walks the batch, a group
+// per lane while whole groups fit and a window per lane inside a group that
+// does not; at a window no summary fits, all threads add it exactly.
 __global__ void __launch_bounds__(kSeqThreads, 1)
     seqclip_chain_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
                          SeqWorkspace ws, SeqClipOut out, uint32_t* kernel_error,
                          SeqCarry* carry, int resume, int finish) {
+  constexpr uint32_t kGroups = kSeqChainBatch / 32;
+  static_assert(kSeqChainBatch == kSeqThreads, "one window per thread when a batch is read");
   __shared__ SeqShared sh;
+  __shared__ uint4 b_total[kSeqChainBatch];
   __shared__ int32_t b_base[kSeqChainBatch];
   __shared__ uint8_t b_flags[kSeqChainBatch];
-  __shared__ uint32_t b_total[kSeqChainBatch * kSeqCand];
-  __shared__ uint32_t s_next, s_miss, s_gbad;
-  const uint32_t t = threadIdx.x;
-  if (t == 0) {
-    seq_begin(sh, carry, resume);
-    s_gbad = 0u;
-  }
+  __shared__ uint4 g_total[kGroups];
+  __shared__ int32_t g_base[kGroups];
+  __shared__ uint32_t g_fit[kGroups];  // bit e: every window fits binade g_base + e
+  __shared__ uint32_t s_next, s_miss;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint4* totals = reinterpret_cast<const uint4*>(ws.total);
+  if (t == 0) seq_begin(sh, carry, resume);
   bool gbad = false;
   for (uint64_t b0 = 0; b0 < n_windows; b0 += kSeqChainBatch) {
     const uint32_t nb = uint32_t(n_windows - b0 < kSeqChainBatch ? n_windows - b0
                                                                   : kSeqChainBatch);
     __syncthreads();  // the previous batch is no longer read
-    for (uint32_t i = t; i < nb; i += kSeqThreads) {
-      b_base[i] = ws.base[b0 + i];
-      b_flags[i] = ws.flags[b0 + i];
+    if (t < nb) {
+      b_total[t] = totals[b0 + t];
+      b_base[t] = ws.base[b0 + t];
+      const uint8_t f = ws.flags[b0 + t];
+      b_flags[t] = f;
+      gbad |= (f & 0x80u) != 0u;  // every window is added, by summary or exactly
     }
-    for (uint32_t i = t; i < nb * kSeqCand; i += kSeqThreads)
-      b_total[i] = ws.total[b0 * kSeqCand + i];
+    __syncthreads();
+    if (32 * warp < nb) {
+      const uint32_t i = 32 * warp + lane;
+      const bool present = i < nb;
+      const int32_t gb = b_base[32 * warp];
+      uint32_t fit = 0u;
+      uint32_t gt[kSeqCand];
+#pragma unroll
+      for (int e = 0; e < kSeqCand; ++e) {
+        bool ok = true;
+        uint32_t tot = 0u;
+        if (present) {
+          const int32_t c = gb + e - b_base[i];
+          ok = c >= 0 && c < kSeqCand && ((b_flags[i] >> c) & 1u) == 0u;
+          if (ok) tot = seq_pick(b_total[i], c);
+        }
+        const uint32_t sum = __reduce_add_sync(kFull, tot);  // 32 x 2^24: no wrap
+        gt[e] = sum < (1u << 24) ? sum : (1u << 24);
+        fit |= __all_sync(kFull, ok) ? (1u << e) : 0u;
+      }
+      if (lane == 0) {
+        g_total[warp] = make_uint4(gt[0], gt[1], gt[2], gt[3]);
+        g_base[warp] = gb;
+        g_fit[warp] = fit;
+      }
+    }
     if (t == 0) s_next = 0u;
     __syncthreads();
     for (;;) {  // block-uniform: s_next and s_miss are read after a barrier
-      if (t == 0) {
+      if (warp == 0) {
         uint32_t k = s_next;
-        uint32_t gb = 0u;
         uint32_t miss = 0u;
-        if (sh.sum_bad) {  // the sum is no longer finite: only the flags matter
-          for (; k < nb; ++k) gb |= b_flags[k];
+        if (sh.sum_bad) {  // the sum is no longer finite: nothing more to add
+          k = nb;
         } else {
+          // Within one binade every window (group) adds its own total, so
+          // the 32 from k are accepted up to the first one that does not fit
+          // this binade or whose running total leaves it.
           const int32_t E = sh.E;
           uint32_t m = sh.m;
-          for (; k < nb; ++k) {
-            const uint32_t f = b_flags[k];
-            gb |= f;
-            const int32_t c = E - b_base[k];
-            if (c < 0 || c >= kSeqCand || ((f >> c) & 1u)) {
-              miss = 1u;
-              break;
+          bool fine = (k & 31u) != 0u;  // inside a group: window by window
+          while (k < nb) {
+            uint32_t tot = 0u, avail;
+            bool ok = false, present;
+            if (fine) {
+              const uint32_t end = ((k | 31u) + 1u) < nb ? ((k | 31u) + 1u) : nb;
+              const uint32_t i = k + lane;
+              avail = end - k;
+              present = i < end;
+              if (present) {
+                const int32_t c = E - b_base[i];
+                ok = c >= 0 && c < kSeqCand && ((b_flags[i] >> c) & 1u) == 0u;
+                if (ok) tot = seq_pick(b_total[i], c);
+              }
+            } else {
+              const uint32_t g0 = k >> 5, ng = (nb + 31u) >> 5;
+              const uint32_t gi = g0 + lane;
+              avail = ng - g0;
+              present = gi < ng;
+              if (present) {
+                const int32_t c = E - g_base[gi];
+                ok = c >= 0 && c < kSeqCand && ((g_fit[gi] >> c) & 1u) != 0u;
+                if (ok) tot = seq_pick(g_total[gi], c);
+              }
             }
-            const uint32_t tot = b_total[k * kSeqCand + c];
-            if (uint64_t(m) + tot >= (1ull << 24)) {
-              miss = 1u;
-              break;
+            uint32_t pre = tot;  // 32 totals of at most 2^24: no wrap
+#pragma unroll
+            for (uint32_t off = 1; off < 32; off <<= 1) {
+              const uint32_t y = __shfl_up_sync(kFull, pre, off);
+              if (lane >= off) pre += y;
             }
-            m += tot;
+            const bool stop = present && (!ok || uint64_t(m) + pre >= (1ull << 24));
+            const uint32_t stops = __ballot_sync(kFull, stop);
+            const uint32_t first = stops ? uint32_t(__ffs(stops)) - 1u : avail;
+            if (first > 0u) m += __shfl_sync(kFull, pre, first - 1u);
+            if (fine) {
+              k += first;
+              if (stops) {  // this window needs the exact procedure
+                miss = 1u;
+                break;
+              }
+              fine = false;  // the group is done
+            } else {
+              k = k + 32u * first < nb ? k + 32u * first : nb;
+              fine = stops != 0u;  // walk the group that did not fit window by window
+            }
           }
-          sh.m = m;
+          if (lane == 0) sh.m = m;
         }
-        s_gbad |= gb & 0x80u;
-        s_next = k;
-        s_miss = miss;
+        if (lane == 0) {
+          s_next = k;
+          s_miss = miss;
+        }
       }
       __syncthreads();
       if (!s_miss) break;
       // The window the summaries could not add: every thread takes its 8 terms.
       const uint64_t w = b0 + s_next;
       float q[kSeqPer];
+      if ((w + 1) * kSeqWindow <= n) {  // a whole window: two 16-byte loads per thread
+        const float4 a = *reinterpret_cast<const float4*>(g + w * kSeqWindow + 8 * t);
+        const float4 c = *reinterpret_cast<const float4*>(g + w * kSeqWindow + 8 * t + 4);
+        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
+        q[4] = c.x; q[5] = c.y; q[6] = c.z; q[7] = c.w;
+      } else {
+#pragma unroll
+        for (uint32_t j = 0; j < kSeqPer; ++j) {
+          const uint64_t i = w * kSeqWindow + 8 * t + j;
+          q[j] = i < n ? g[i] : 0.0f;
+        }
+      }
 #pragma unroll
       for (uint32_t j = 0; j < kSeqPer; ++j) {
-        const uint64_t i = w * kSeqWindow + 8 * t + j;
-        const float x = i < n ? g[i] : 0.0f;
-        gbad |= !finite_f32(x);
-        q[j] = __fmul_rn(x, x);
+        gbad |= !finite_f32(q[j]);
+        q[j] = __fmul_rn(q[j], q[j]);
       }
       seq_window_exact(sh, q);
       if (t == 0) s_next += 1u;
       __syncthreads();
     }
   }
-  const bool any_bad = __syncthreads_or(gbad ? 1 : 0) || s_gbad || sh.gbad_before;
+  const bool any_bad = __syncthreads_or(gbad ? 1 : 0) || sh.gbad_before;
   if (t == 0) seq_store(sh, any_bad, true, out, kernel_error, carry, finish);
 }
 
@@ -1859,6 +2023,12 @@ __global__ void validate_state_kernel(const float* __restrict__ master,
 #endif
 #ifndef SLM_PEER_STAGE_BYTES
 #define SLM_PEER_STAGE_BYTES 32768
+#endif
+#ifndef SLM_PEER_BATCH2
+#define SLM_PEER_BATCH2 4  // tree rows in flight per thread at world <= 2
+#endif
+#ifndef SLM_PEER_MINBLOCKS2
+#define SLM_PEER_MINBLOCKS2 4  // resident blocks per SM asked of the compiler at world <= 2
 #endif
 constexpr bool kPeerLoads = SLM_PEER_LOADS != 0;     // plain loads instead of bulk copies
 constexpr uint32_t kPeerStages = SLM_PEER_STAGES;
@@ -2009,8 +2179,8 @@ __device__ __forceinline__ double peer_chunk_ragged(const PeerTable& pt, int wor
 
 // kBatch == 0: bulk copies through shared memory; otherwise plain loads,
 // kBatch rows x kRanks ranks in flight per thread.
-template <typename GT, int kBatch, int kRanks>
-__global__ void __launch_bounds__(kTreeThreads)
+template <typename GT, int kBatch, int kRanks, int kMinBlocks = 1>
+__global__ void __launch_bounds__(kTreeThreads, kMinBlocks)
     zero1_peer_reduce_kernel(PeerTable pt, int rank, int world, uint64_t shard_begin,
                              uint64_t n_valid, uint32_t n_chunks, const DeviceScaler* scaler,
                              FinalizeParams fp, float* __restrict__ gsum, uint32_t rows,
@@ -2526,18 +2696,18 @@ cudaError_t launch_zero1_peer_reduce(int dtype, const PeerTable& pt, int rank, i
   if (n_chunks == 0 || world < 1 || world > kMaxRanks) return cudaErrorInvalidValue;
   if constexpr (kPeerLoads) {
     // Plain loads: B rows x R ranks in flight per thread (8 loads per batch).
-#define SLM_PEER_LAUNCH(GT, B, R)                                                             \
-  zero1_peer_reduce_kernel<GT, B, R><<<n_chunks, kTreeThreads, 0, stream>>>(                  \
+#define SLM_PEER_LAUNCH(GT, B, R, M)                                                          \
+  zero1_peer_reduce_kernel<GT, B, R, M><<<n_chunks, kTreeThreads, 0, stream>>>(               \
       pt, rank, world, shard_begin, n_valid, n_chunks, scaler, fp, gsum, 0u, 0u, epoch, st,  \
       timeout_ns)
     if (dtype == 0) {
-      if (world <= 2) SLM_PEER_LAUNCH(float, 4, 2);
-      else if (world <= 4) SLM_PEER_LAUNCH(float, 2, 4);
-      else SLM_PEER_LAUNCH(float, 1, 8);
+      if (world <= 2) SLM_PEER_LAUNCH(float, 4, 2, 1);
+      else if (world <= 4) SLM_PEER_LAUNCH(float, 2, 4, 1);
+      else SLM_PEER_LAUNCH(float, 1, 8, 1);
     } else {
-      if (world <= 2) SLM_PEER_LAUNCH(uint16_t, 4, 2);
-      else if (world <= 4) SLM_PEER_LAUNCH(uint16_t, 2, 4);
-      else SLM_PEER_LAUNCH(uint16_t, 1, 8);
+      if (world <= 2) SLM_PEER_LAUNCH(uint16_t, SLM_PEER_BATCH2, 2, SLM_PEER_MINBLOCKS2);
+      else if (world <= 4) SLM_PEER_LAUNCH(uint16_t, 2, 4, 1);
+      else SLM_PEER_LAUNCH(uint16_t, 1, 8, 1);
     }
 #undef SLM_PEER_LAUNCH
     return cudaGetLastError();
@@ -2648,10 +2818,11 @@ cudaError_t launch_sequential_clip(const float* g, uint64_t n, const SeqClipOut&
       return cudaErrorInvalidValue;
     uint8_t* base = static_cast<uint8_t*>(workspace);
     SeqWorkspace ws;
-    ws.sums = reinterpret_cast<double*>(base);
-    ws.base = reinterpret_cast<int32_t*>(base + n_windows * sizeof(double));
-    ws.total = reinterpret_cast<uint32_t*>(base + n_windows * (sizeof(double) + sizeof(int32_t)));
-    ws.flags = base + n_windows * (sizeof(double) + sizeof(int32_t) + kSeqCand * sizeof(uint32_t));
+    ws.total = reinterpret_cast<uint32_t*>(base);
+    ws.sums = reinterpret_cast<double*>(base + n_windows * kSeqCand * sizeof(uint32_t));
+    ws.base = reinterpret_cast<int32_t*>(base + n_windows * (kSeqCand * sizeof(uint32_t) +
+                                                            sizeof(double)));
+    ws.flags = base + n_windows * (kSeqCand * sizeof(uint32_t) + sizeof(double) + sizeof(int32_t));
     const uint64_t cap = uint64_t(current_sms()) * 8;
     const unsigned grid = unsigned(n_windows < cap ? n_windows : cap);
     seqclip_sums_kernel<<<grid, kSeqPassThreads, 0, stream>>>(g, n, n_windows, ws);

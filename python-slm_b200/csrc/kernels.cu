@@ -1740,7 +1740,7 @@ __device__ __forceinline__ float seq_pow2(int32_t k) {
 // exactly one half (a tie, which the chain resolves term by term).  In f32:
 // y = q / 2^E is exact (a power-of-two scaling; an overflow means y >= 2^24
 // anyway, an underflow means y < 2^-126, an increment of 0 that cannot tie),
-// rint(y) is the increment wherever there is no tie, y - rint(y) is exact
+// rintf(y) is the increment wherever there is no tie, y - rintf(y) is exact
 // and is +-0.5 exactly at a tie, and an f32 running total of non-negative
 // integers is exact below 2^24 and stays >= 2^24 once the exact total gets
 // there -- all the chain needs (totals are clamped at 2^24).  An infinite or
@@ -1764,10 +1764,7 @@ __global__ void __launch_bounds__(kSeqPassThreads)
       float y = __fmul_rn(__fmul_rn(__fmul_rn(x[j], x[j]), s0), s1);
 #pragma unroll
       for (int c = 0; c < kSeqCand; ++c) {
-        // rint(y) without the conversion unit: below 2^23, y + 2^23 lands
-        // where the f32 spacing is 1 and rounds to nearest-even there (2^23 is
-        // even); from 2^23 on, y is an integer already (inf and NaN pass).
-        const float r = y < 8388608.0f ? __fsub_rn(__fadd_rn(y, 8388608.0f), 8388608.0f) : y;
+        const float r = rintf(y);
         tot[c] = __fadd_rn(tot[c], r);
         dev[c] = fmaxf(dev[c], fabsf(__fsub_rn(y, r)));
         y = __fmul_rn(y, 0.5f);

@@ -1582,6 +1582,10 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
 // binades are candidates affects only how many windows take the exact path,
 // never the result.
 constexpr int kSeqCand = 4;
+#ifndef SLM_SEQ_XU_CANDS
+#define SLM_SEQ_XU_CANDS 3
+#endif
+constexpr int kSeqXuCands = SLM_SEQ_XU_CANDS;  // candidates rounded with rintf
 constexpr uint32_t kSeqPassThreads = 256;
 constexpr uint32_t kSeqChainBatch = 1024;  // window summaries per shared-memory batch
 
@@ -1764,7 +1768,13 @@ __global__ void __launch_bounds__(kSeqPassThreads)
       float y = __fmul_rn(__fmul_rn(__fmul_rn(x[j], x[j]), s0), s1);
 #pragma unroll
       for (int c = 0; c < kSeqCand; ++c) {
-        const float r = rintf(y);
+        // rintf issues on the conversion unit; the first kSeqXuCands
+        // candidates use it, the rest round by adding and removing 2^23 (below
+        // 2^23, y + 2^23 lands where the f32 spacing is 1 and rounds to
+        // nearest-even there, 2^23 being even; from 2^23 on y is an integer
+        // already, inf and NaN pass), which spreads the work over two pipes.
+        const float r = c < kSeqXuCands ? rintf(y)
+                        : (y < 8388608.0f ? __fsub_rn(__fadd_rn(y, 8388608.0f), 8388608.0f) : y);
         tot[c] = __fadd_rn(tot[c], r);
         dev[c] = fmaxf(dev[c], fabsf(__fsub_rn(y, r)));
         y = __fmul_rn(y, 0.5f);

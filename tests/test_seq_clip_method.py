@@ -293,3 +293,20 @@ def test_f32_candidate_totals_equal_integer_increments():
                 assert np.array_equal(ties[:, c], per_window_tie)
                 want = np.minimum(r.reshape(4, W).sum(axis=1), TWO24)
                 assert np.array_equal(totals[~per_window_tie, c], want[~per_window_tie])
+
+
+def test_add_based_rounding_is_rint():
+    # The candidate kernel rounds some candidates by y + 2^23 - 2^23 below
+    # 2^23 (y itself from there on) instead of rintf: the same value for
+    # every f32 y >= 0, ties to even included.
+    rng = np.random.default_rng(9)
+    two23 = F(8388608.0)
+    ys = np.concatenate([
+        rng.uniform(0, 2**24, 1_000_000).astype(F),
+        (rng.integers(0, 2**25, 1_000_000) / 2.0).astype(F),   # every half
+        (2.0 ** rng.uniform(-40, 30, 1_000_000)).astype(F),
+        np.array([0, 0.5, 1.5, 2.5, 8388607.5, 8388608, 8388609, 16777215, 16777216,
+                  3e38, np.inf], F)])
+    with np.errstate(over="ignore"):
+        r = np.where(ys < two23, ((ys + two23).astype(F) - two23).astype(F), ys)
+    assert np.array_equal(r, np.rint(ys))

@@ -1299,7 +1299,7 @@ struct SeqShared {
   uint32_t m;
   uint32_t sum_bad;    // ... unless it became non-finite (then sum_bits holds it)
   float sum_bits;
-  uint32_t restart, stop, total;
+  uint32_t restart[2];  // by pass parity: a pass's value is read before it is reset
   uint32_t fast_total[2], fast_tie[2];
   uint32_t gbad_before;  // a non-finite gradient in an earlier slice
 };
@@ -1325,70 +1325,82 @@ __device__ __forceinline__ void seq_begin(SeqShared& sh, const SeqCarry* carry, 
 // finds the first term that ties or leaves the binade, the prefix before it
 // is applied, that term is added with a real f32 add, and the rest of the
 // window is redone with the new binade.  Called by all threads of the CTA.
+// Two barriers per pass: each warp publishes its total (thread totals
+// clamped at 2^24, which keeps every sum below 2^29 and every comparison with
+// 2^24 - m as it was) and its first tie; then every warp scans the 32 warp
+// summaries itself, so all threads know the first tie and the first warp
+// whose running total leaves the binade, and only that warp looks for the
+// exact term.  The one thread owning the stopping term publishes the new sum
+// and where to resume; `restart` defaults to the window's end, so every pass
+// moves forward (two slots by pass parity: thread 0 resets the next pass's
+// slot while others may still read this one's).
 __device__ __forceinline__ void seq_window_exact(SeqShared& sh, const float (&q)[kSeqPer]) {
+  constexpr uint32_t kWarps = kSeqThreads / 32;
+  constexpr uint32_t kWarpTerms = 32 * kSeqPer;
+  static_assert(kWarps == 32, "one lane per warp in the block-wide scans");
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
-  uint32_t* warp_val = sh.warp_val;
-  uint32_t* warp_stop = sh.warp_stop;
   uint32_t start = 0;  // first term of the window not yet added
-  for (;;) {           // block-uniform: every value below is read after a barrier
+  for (uint32_t pass = 0; pass <= kSeqWindow; ++pass) {  // block-uniform
     if (sh.sum_bad) break;
     const int32_t E = sh.E;
     const uint32_t m = sh.m;
-    uint32_t pre[kSeqPer], run = 0, stop = kNoStop;
+    uint32_t pre[kSeqPer], run = 0, tie_at = kNoStop;
 #pragma unroll
     for (uint32_t j = 0; j < kSeqPer; ++j) {
       const uint32_t idx = 8 * t + j;
       bool tie = false;
       const uint32_t r = idx < start ? 0u : seq_increment(q[j], E, tie);
-      run += r;
+      run += r;  // 8 x 2^25 at most
       pre[j] = run;
-      if (tie && stop == kNoStop) stop = idx;
+      if (tie && tie_at == kNoStop) tie_at = idx;
     }
-    // exclusive prefix of the thread totals over the block
-    uint32_t incl = run;
+    const uint32_t runc = run < (1u << 24) ? run : (1u << 24);
+    uint32_t incl = runc;  // this warp's inclusive prefix of clamped thread totals
 #pragma unroll
     for (uint32_t off = 1; off < 32; off <<= 1) {
       const uint32_t y = __shfl_up_sync(kFull, incl, off);
       if (lane >= off) incl += y;
     }
-    if (lane == 31) warp_val[warp] = incl;
+    const uint32_t wtie = __reduce_min_sync(kFull, tie_at);
+    if (lane == 31) sh.warp_val[warp] = incl < (1u << 24) ? incl : (1u << 24);
+    if (lane == 0) sh.warp_stop[warp] = wtie;
+    uint32_t& restart = sh.restart[pass & 1u];
+    if (t == 0) restart = kSeqWindow;
     __syncthreads();
-    if (warp == 0) {
-      uint32_t v = warp_val[lane];
+    uint32_t scan = sh.warp_val[lane];  // lane l: inclusive total through warp l
 #pragma unroll
-      for (uint32_t off = 1; off < 32; off <<= 1) {
-        const uint32_t y = __shfl_up_sync(kFull, v, off);
-        if (lane >= off) v += y;
-      }
-      warp_val[lane] = v;
+    for (uint32_t off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFull, scan, off);
+      if (lane >= off) scan += y;
     }
-    __syncthreads();
-    const uint32_t excl = (incl - run) + (warp ? warp_val[warp - 1] : 0u);
-    const uint32_t total = warp_val[31];
-    // first term whose running sum would leave the binade (exact up to it)
-#pragma unroll
-    for (uint32_t j = 0; j < kSeqPer; ++j) {
-      const uint32_t idx = 8 * t + j;
-      if (idx >= start && idx < stop && uint64_t(m) + excl + pre[j] >= (1ull << 24)) stop = idx;
-    }
-    const uint32_t wmin = __reduce_min_sync(kFull, stop);
-    if (lane == 0) warp_stop[warp] = wmin;
-    __syncthreads();
-    if (warp == 0) {
-      const uint32_t v = __reduce_min_sync(kFull, warp_stop[lane]);
-      if (lane == 0) {
-        sh.stop = v;
-        sh.total = total;
-      }
-    }
-    __syncthreads();
-    const uint32_t first = sh.stop;
-    if (first == kNoStop) {  // the whole rest of the window stays in the binade
-      if (t == 0) sh.m = m + sh.total;
+    const uint32_t first_tie = __reduce_min_sync(kFull, sh.warp_stop[lane]);
+    const uint32_t leaves = __ballot_sync(kFull, uint64_t(m) + scan >= (1ull << 24));
+    const uint32_t wstar = leaves ? uint32_t(__ffs(leaves)) - 1u : kWarps;
+    const uint32_t total = __shfl_sync(kFull, scan, 31);
+    if (wstar == kWarps && first_tie == kNoStop) {  // the rest stays in the binade
+      if (t == 0) sh.m = m + total;
       __syncthreads();
       break;
     }
-    if (first >= 8 * t && first < 8 * t + kSeqPer) {  // the owner of the stopping term
+    // The stop is the first tie if it comes before warp wstar's terms; else
+    // it lies in warp wstar (its first tie or its first term leaving the binade).
+    const bool in_wstar = wstar < kWarps && first_tie >= kWarpTerms * wstar;
+    const uint32_t below = __shfl_sync(kFull, scan, warp ? warp - 1u : 0u);
+    const uint32_t excl = (warp ? below : 0u) + (incl - runc);  // exact up to the stop
+    uint32_t first = first_tie;
+    if (in_wstar && warp == wstar) {
+      uint32_t cross = kNoStop;
+#pragma unroll
+      for (uint32_t j = 0; j < kSeqPer; ++j) {
+        const uint32_t idx = 8 * t + j;
+        if (idx >= start && cross == kNoStop && uint64_t(m) + excl + pre[j] >= (1ull << 24))
+          cross = idx;
+      }
+      const uint32_t c = __reduce_min_sync(kFull, cross);
+      first = c < first_tie ? c : first_tie;
+    }
+    const bool knows = !in_wstar || warp == wstar;
+    if (knows && first >= 8 * t && first < 8 * t + kSeqPer) {  // the owner of the stop
       const uint32_t j0 = first - 8 * t;
       uint32_t before = excl;
       float qj = 0.0f;
@@ -1408,10 +1420,10 @@ __device__ __forceinline__ void seq_window_exact(SeqShared& sh, const float (&q)
         sh.E = E2;
         sh.m = m2;
       }
-      sh.restart = first + 1;
+      restart = first + 1;
     }
     __syncthreads();
-    start = sh.restart;
+    start = restart;
     if (start >= kSeqWindow) break;
   }
 }

@@ -310,3 +310,60 @@ def test_add_based_rounding_is_rint():
     with np.errstate(over="ignore"):
         r = np.where(ys < two23, ((ys + two23).astype(F) - two23).astype(F), ys)
     assert np.array_equal(r, np.rint(ys))
+
+
+def _first_stop_two_level(q: np.ndarray, E: int, m: int, start: int) -> int:
+    """The device's stop search in one pass of the exact procedure: thread
+    totals (8 terms) and warp totals (32 threads) clamped at 2^24, the first
+    warp whose running total reaches 2^24 - m, the first tie, and the exact
+    term looked up only inside that warp."""
+    r, tie = increments(q, E)
+    idx = np.arange(q.size)
+    r = np.where(idx < start, 0, r)
+    tie = tie & (idx >= start)
+    per = r.reshape(1024, 8)
+    pre = np.cumsum(per, axis=1)                      # inclusive within a thread
+    runc = np.minimum(pre[:, -1], TWO24)
+    warp_incl = np.cumsum(runc.reshape(32, 32), axis=1)   # within each warp
+    warp_tot = np.minimum(warp_incl[:, -1], TWO24)
+    scan = np.cumsum(warp_tot)
+    first_tie = int(np.flatnonzero(tie)[0]) if tie.any() else None
+    leaves = np.flatnonzero(m + scan >= TWO24)
+    wstar = int(leaves[0]) if leaves.size else None
+    if wstar is None:
+        return first_tie if first_tie is not None else -1
+    if first_tie is not None and first_tie < 256 * wstar:
+        return first_tie
+    below = int(scan[wstar - 1]) if wstar else 0
+    excl_in_warp = warp_incl[wstar] - runc.reshape(32, 32)[wstar]
+    for lane in range(32):
+        th = 32 * wstar + lane
+        excl = below + int(excl_in_warp[lane])
+        for j in range(8):
+            k = 8 * th + j
+            if k >= start and m + excl + int(pre[th, j]) >= TWO24:
+                return k if first_tie is None else min(k, first_tie)
+    raise AssertionError("the warp whose total leaves the binade holds the crossing")
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_clamped_two_level_search_finds_the_first_stop(seed):
+    # Huge terms (whose increments would wrap 32-bit sums) mixed with small
+    # ones, at several binades and resume points: the clamped search must
+    # stop exactly where the plain running sum says.
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(W) * 1e-3).astype(F)
+    x[rng.integers(0, W, 40)] = F(1e6)
+    x[rng.integers(0, W, 40)] = (2.0 ** rng.integers(-30, 0, 40)).astype(F)
+    q = (x * x).astype(F)
+    for E in (-149, -60, -40, -30, -20, 10):
+        for m in (0, 1 << 23, TWO24 - 5):
+            for start in (0, 1, 4097, W - 3):
+                r, tie = increments(q, E)
+                idx = np.arange(W)
+                r = np.where(idx < start, 0, r)
+                tie = tie & (idx >= start)
+                cum = np.cumsum(r)
+                stops = np.flatnonzero(tie | ((m + cum >= TWO24) & (idx >= start)))
+                want = int(stops[0]) if stops.size else -1
+                assert _first_stop_two_level(q, E, m, start) == want, (E, m, start)

@@ -2,6 +2,7 @@
 // codec, the fused step, the strict apply_update drop-in, the state hash.
 // The ZeRO-1 collectives live in zero1.cu.
 #include "handle.h"
+#include "hostcopy.h"
 #include "sha256.h"
 
 #include <algorithm>
@@ -312,7 +313,7 @@ int stage_pageable(slm_opt_handle* h, void* dst, const void* src, size_t bytes,
       const size_t part = (len + T - 1) / T;
       const size_t lo = std::min(len, w * part), hi = std::min(len, lo + part);
       if (lo < hi)
-        std::memcpy(static_cast<uint8_t*>(h->ring.slot[c % Ring::kSlots]) + lo,
+        stream_copy(static_cast<uint8_t*>(h->ring.slot[c % Ring::kSlots]) + lo,
                     static_cast<const uint8_t*>(src) + off + lo, hi - lo);
       parts[c].fetch_add(1, std::memory_order_acq_rel);
     }

@@ -27,8 +27,8 @@ INCLUDE = REPO_ROOT / "include"
 LIB_NAME = "libslmopt.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["kernels.cu", "api.cu", "zero1.cu", "noalloc.cu", "sha256.cpp"]
-HEADERS = ["slmopt_internal.h", "handle.h", "sha256.h"]
+SOURCES = ["kernels.cu", "api.cu", "zero1.cu", "noalloc.cu", "sha256.cpp", "hostcopy.cpp"]
+HEADERS = ["slmopt_internal.h", "handle.h", "sha256.h", "hostcopy.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -183,3 +183,23 @@ def test_clip_workspace_size_and_validation_without_a_device():
     st = lib.slm_gradient_clip_scale_ws(grads, 10 * 8192, ws + 8, need, out, None)
     assert st == _lib.SLM_ERR_INVALID_ARGUMENT
     assert "align" in lib.slm_last_error_message().decode()
+
+
+def test_staging_copy_is_exact_at_every_alignment_and_size():
+    # The host copy that fills the pinned staging ring (non-temporal stores for
+    # large copies where the CPU has AVX2) must move every byte, whatever the
+    # alignment of either side and whatever the tail.
+    import numpy as np
+
+    lib = _lib.load()
+    fn = getattr(lib, "_ZN6slmopt11stream_copyEPvPKvm")
+    fn.restype = None
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+    rng = np.random.default_rng(4)
+    src = rng.integers(0, 256, (1 << 20) + 300, dtype=np.uint8)
+    for n in (0, 1, 31, 4096, (1 << 16) - 1, 1 << 16, (1 << 16) + 77, (1 << 20) + 129):
+        for so, do in ((0, 0), (1, 0), (0, 7), (13, 29), (32, 5)):
+            dst = np.zeros(n + 64, np.uint8)
+            fn(dst.ctypes.data + do, src.ctypes.data + so, n)
+            assert np.array_equal(dst[do:do + n], src[so:so + n]), (n, so, do)
+            assert not dst[:do].any() and not dst[do + n:].any(), (n, so, do)

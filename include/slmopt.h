@@ -258,10 +258,12 @@ int slm_opt_update_pass(slm_opt_handle* h, const slm_step_config* cfg, void* str
  * (gradient_clip_scale, src/model/oracle.rs:486-507, reproduced bit for bit
  * on the device, so the accept / reject decision is the reference's even where
  * that sum drifts from the exact one; see slm_gradient_clip_scale); from
- * pageable host memory the gradients travel through a pinned ring filled by
- * host threads and the check runs slice by slice as they land; the lr must
- * bit-equal
- * canonical_learning_rate(t) (P12_SCHEDULER_STATE_MISMATCH); AdamW runs with
+ * pageable host memory the gradients travel through a pinned ring of three
+ * 32 MB slots filled by host threads with streaming stores (half the host's
+ * hardware threads, at most 8; the environment variable SLM_STAGING_THREADS,
+ * 1..64, overrides), and the check runs slice by slice as they land; the lr
+ * must bit-equal canonical_learning_rate(t) (P12_SCHEDULER_STATE_MISMATCH);
+ * AdamW runs with
  * OPT-001's constants and no further clip.  `grads_host` is host f32[n].
  * valid_targets is accepted and unused, as in the reference.  If out_sha256
  * is non-NULL it receives the post-update state SHA-256 (slow, off-path). */

@@ -1585,19 +1585,28 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
 // While the sum stays in a binade, a whole window adds an integer number of
 // ulps that depends only on that binade.  So windows are summarised in
 // parallel first -- for each, its total increment and tie flag under the
-// kSeqCand binades the running sum can plausibly be in there (around the
-// binade of the window's exact f64 prefix sum, since the in-order f32 sum
-// drifts from it by well under a factor of 4 in practice) -- and one CTA
+// kSeqCandUsed binades the running sum can plausibly be in there (the binade
+// of the window's exact f64 prefix sum and its neighbours: the in-order f32
+// sum drifts from that prefix by well under a factor of 2 in practice) -- and one CTA
 // then chains the windows in order through those summaries, adding the exact
 // window procedure above only where the sum's binade is not among the
 // candidates, a term ties, or the window's total leaves the binade.  Which
 // binades are candidates affects only how many windows take the exact path,
 // never the result.
-constexpr int kSeqCand = 4;
-#ifndef SLM_SEQ_XU_CANDS
-#define SLM_SEQ_XU_CANDS 3
+constexpr int kSeqCand = 4;  // slots per window record
+#ifndef SLM_SEQ_CANDS
+#define SLM_SEQ_CANDS 3  // candidate binades computed (the rest of the record never fits)
 #endif
+#ifndef SLM_SEQ_CAND_BELOW
+#define SLM_SEQ_CAND_BELOW 1  // the first candidate's distance below the prefix's binade
+#endif
+#ifndef SLM_SEQ_XU_CANDS
+#define SLM_SEQ_XU_CANDS 2
+#endif
+constexpr int kSeqCandUsed = SLM_SEQ_CANDS;
+constexpr int kSeqCandBelow = SLM_SEQ_CAND_BELOW;
 constexpr int kSeqXuCands = SLM_SEQ_XU_CANDS;  // candidates rounded with rintf
+static_assert(kSeqCandUsed >= 1 && kSeqCandUsed <= kSeqCand, "1..4 candidates per record");
 constexpr uint32_t kSeqPassThreads = 256;
 constexpr uint32_t kSeqChainBatch = 1024;  // window summaries per shared-memory batch
 
@@ -1739,7 +1748,7 @@ __global__ void __launch_bounds__(kSeqThreads)
       }
       const uint64_t idx = w_lo + (j0 + j) * 32 + lane;
       if (j0 + j < steps && idx < n_windows)
-        ws.base[idx] = seq_binade(float(run + (incl - v[j]))) - (kSeqCand / 2);
+        ws.base[idx] = seq_binade(float(run + (incl - v[j]))) - kSeqCandBelow;
       run += __shfl_sync(kFull, incl, 31);
     }
   }
@@ -1764,7 +1773,7 @@ __device__ __forceinline__ float seq_pow2(int32_t k) {
 __global__ void __launch_bounds__(kSeqPassThreads)
     seqclip_candidates_kernel(const float* __restrict__ g, uint64_t n, uint64_t n_windows,
                               SeqWorkspace ws) {
-  __shared__ uint32_t wtot[kSeqCand][kSeqPassThreads / 32];
+  __shared__ uint32_t wtot[kSeqCandUsed][kSeqPassThreads / 32];
   __shared__ uint32_t wtie[kSeqPassThreads / 32];
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   for (uint64_t w = blockIdx.x; w < n_windows; w += gridDim.x) {
@@ -1774,12 +1783,12 @@ __global__ void __launch_bounds__(kSeqPassThreads)
     const bool split = k > 127;
     const float s0 = seq_pow2(split ? k - 64 : (k < -149 ? -149 : k));
     const float s1 = split ? seq_pow2(64) : 1.0f;
-    float tot[kSeqCand] = {}, dev[kSeqCand] = {};
+    float tot[kSeqCandUsed] = {}, dev[kSeqCandUsed] = {};
 #pragma unroll
     for (uint32_t j = 0; j < kSeqWindow / kSeqPassThreads; ++j) {
       float y = __fmul_rn(__fmul_rn(__fmul_rn(x[j], x[j]), s0), s1);
 #pragma unroll
-      for (int c = 0; c < kSeqCand; ++c) {
+      for (int c = 0; c < kSeqCandUsed; ++c) {
         // rintf issues on the conversion unit; the first kSeqXuCands
         // candidates use it, the rest round by adding and removing 2^23 (below
         // 2^23, y + 2^23 lands where the f32 spacing is 1 and rounds to
@@ -1794,7 +1803,7 @@ __global__ void __launch_bounds__(kSeqPassThreads)
     }
     uint32_t ties = 0;
 #pragma unroll
-    for (int c = 0; c < kSeqCand; ++c) {
+    for (int c = 0; c < kSeqCandUsed; ++c) {
       const uint32_t v = tot[c] < 16777216.0f ? uint32_t(tot[c]) : (1u << 24);  // NaN too
       const uint32_t sum = __reduce_add_sync(kFull, v);  // 32 x 2^24: no wrap
       if (lane == 0) wtot[c][warp] = sum < (1u << 24) ? sum : (1u << 24);
@@ -1803,9 +1812,12 @@ __global__ void __launch_bounds__(kSeqPassThreads)
     const uint32_t tw = __reduce_or_sync(kFull, ties);
     if (lane == 0) wtie[warp] = tw;
     __syncthreads();
-    if (t < kSeqCand) {
-      uint32_t v = 0;
-      for (uint32_t i = 0; i < kSeqPassThreads / 32; ++i) v += wtot[t][i];
+    if (t < kSeqCand) {  // slots past the used candidates never fit
+      uint32_t v = 1u << 24;
+      if (t < uint32_t(kSeqCandUsed)) {
+        v = 0;
+        for (uint32_t i = 0; i < kSeqPassThreads / 32; ++i) v += wtot[t][i];
+      }
       ws.total[w * kSeqCand + t] = v < (1u << 24) ? v : (1u << 24);
     }
     if (t == 0) {
@@ -1859,14 +1871,14 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
       const bool present = i < nb;
       const int32_t gb = b_base[32 * warp];
       uint32_t fit = 0u;
-      uint32_t gt[kSeqCand];
+      uint32_t gt[kSeqCand] = {1u << 24, 1u << 24, 1u << 24, 1u << 24};
 #pragma unroll
-      for (int e = 0; e < kSeqCand; ++e) {
+      for (int e = 0; e < kSeqCandUsed; ++e) {
         bool ok = true;
         uint32_t tot = 0u;
         if (present) {
           const int32_t c = gb + e - b_base[i];
-          ok = c >= 0 && c < kSeqCand && ((b_flags[i] >> c) & 1u) == 0u;
+          ok = c >= 0 && c < kSeqCandUsed && ((b_flags[i] >> c) & 1u) == 0u;
           if (ok) tot = seq_pick(b_total[i], c);
         }
         const uint32_t sum = __reduce_add_sync(kFull, tot);  // 32 x 2^24: no wrap
@@ -1904,7 +1916,7 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
               present = i < end;
               if (present) {
                 const int32_t c = E - b_base[i];
-                ok = c >= 0 && c < kSeqCand && ((b_flags[i] >> c) & 1u) == 0u;
+                ok = c >= 0 && c < kSeqCandUsed && ((b_flags[i] >> c) & 1u) == 0u;
                 if (ok) tot = seq_pick(b_total[i], c);
               }
             } else {
@@ -1914,7 +1926,7 @@ __global__ void __launch_bounds__(kSeqThreads, 1)
               present = gi < ng;
               if (present) {
                 const int32_t c = E - g_base[gi];
-                ok = c >= 0 && c < kSeqCand && ((g_fit[gi] >> c) & 1u) != 0u;
+                ok = c >= 0 && c < kSeqCandUsed && ((g_fit[gi] >> c) & 1u) != 0u;
                 if (ok) tot = seq_pick(g_total[gi], c);
               }
             }

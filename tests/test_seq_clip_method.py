@@ -11,7 +11,7 @@ pinned without a GPU:
 * while the sum s = m * 2^E stays in one binade, fl(s + q) = (m + r) * 2^E
   with r = q / 2^E rounded to the nearest integer, unless q / 2^E is exactly
   halfway (a tie) or m + r reaches 2^24 (the binade changes);
-* per 8,192-term window, for the 4 binades from a base taken from the exact
+* per 8,192-term window, for the 3 binades around the binade of the exact
   f64 prefix sum, the window's total of r in f32 (per thread of 256, then
   clamped integers) and its tie flags;
 * a walk over groups of 32 windows, then windows, accepting totals while
@@ -30,7 +30,8 @@ import slm_oracle as oracle
 F = np.float32
 W = 8192            # terms per window
 THREADS = 256       # threads of the candidate pass
-NC = 4              # candidate binades per window
+NC = 3              # candidate binades per window
+BELOW = 1           # the first candidate's distance below the prefix's binade
 BATCH = 1024        # window summaries per chain batch
 TWO24 = 1 << 24
 
@@ -90,7 +91,7 @@ def seq_binade(s: np.float32) -> int:
 
 
 def candidate_pass(q: np.ndarray, base: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
-    """Per window: 4 clamped totals and tie bits, the way the candidate
+    """Per window: NC clamped totals and tie bits, the way the candidate
     kernel forms them (thread t holds float4s t + 256k, k = 0..7; its terms
     are added in f32 in that order)."""
     nw = base.size
@@ -135,7 +136,7 @@ def chain_sum(g: np.ndarray, base_shift: np.ndarray | None = None) -> tuple[bool
     sums = q.reshape(nw, W).astype(np.float64).sum(axis=1)
     prefix = np.concatenate([[0.0], np.cumsum(sums)[:-1]])
     with np.errstate(over="ignore"):  # an f64 prefix beyond f32 reads as inf
-        base = np.array([seq_binade(F(p)) for p in prefix], np.int64) - NC // 2
+        base = np.array([seq_binade(F(p)) for p in prefix], np.int64) - BELOW
     if base_shift is not None:
         base = base + base_shift
     totals, ties = candidate_pass(q, base)

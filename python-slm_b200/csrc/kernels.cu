@@ -1831,7 +1831,7 @@ __global__ void __launch_bounds__(kSeqPassThreads)
 
 // One CTA chains the window summaries in order.  A batch of 1,024 windows is
 // read into shared memory and summarised once more per group of 32 windows
-// (warp j: group j): for each of the 4 binades from the group's first base,
+// (warp j: group j): for each candidate binade from the group's first base,
 // the group's total and whether every window of the group has that binade
 // among its candidates without a tie.  Warp 0 then walks the batch, a group
 // per lane while whole groups fit and a window per lane inside a group that

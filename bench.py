@@ -29,6 +29,13 @@ written by ``tests/golden/make_step_golden.py``), plus one step with an
 injected +inf that must be skipped; the line carries the outcome as
 ``parity`` and the run exits non-zero on a mismatch.
 
+For N > 1 the line also replays the 100-update dynamic-loss-scale stress run
+against the oracle's trajectory (``stress``).  For N = 1 at full size it also
+times the reference's own drop-in, ``slm_opt_apply_update`` (pageable host
+f32 gradients, the reference's sequential clip re-check reproduced on the
+device, AdamW), and that clip check alone in both device forms
+(``apply_update``).
+
 ``--nvlink-peak`` (one process, ``--gpus N`` devices) measures the peer-copy
 bandwidth the ZeRO-1 roofline is quoted against instead of benchmarking.
 """
@@ -55,9 +62,8 @@ FALLBACK_HBM_GBS = 6650.0
 UPDATE_BYTES = {"mixed": 28, "fp32": 30}
 STEP_BYTES = {"mixed": 30, "fp32": 34}  # + the norm pass's read of g
 # dram__bytes_read.sum + dram__bytes_write.sum of one full-size update-kernel
-# launch (135,285,504 params, one-pass ncu capture, cold cache), from
-# profiles/step_kernels_traffic_135m_mixed.md and
-# profiles/step_kernels_traffic_135m_fp32.md.
+# launch (135,285,504 params, one-pass ncu capture, cold cache), one capture
+# per workload; the summaries of those captures are kept under profiles/.
 UPDATE_TRAFFIC_BYTES = {"mixed": 3.725e9, "fp32": 3.996e9}
 # ... and of the whole step (the norm pass's launch added).
 STEP_TRAFFIC_BYTES = {"mixed": 3.9998e9, "fp32": 4.5408e9}

@@ -360,7 +360,7 @@ def ctypes_lr(lib, t: int) -> float:
 
 
 def run_nvlink_peak(args) -> None:
-    """Peer-copy bandwidth between this box's GPUs: cudaMemcpyPeerAsync on
+    """Peer-copy bandwidth between this machine's GPUs: cudaMemcpyPeerAsync on
     copy engines, one non-blocking stream per (source, destination) pair
     created on the destination device, peer access enabled both ways.
 
@@ -672,7 +672,7 @@ def run_single(args) -> None:
     e2e_ms = (time.perf_counter() - t0) * 1e3 / E
     # Both are the public API with every step's gradients copied in and its
     # result read back; the line reports the faster (which one wins depends on
-    # the box's PCIe and host-memory behaviour) and keeps both.
+    # the machine's PCIe and host-memory behaviour) and keeps both.
     pipelined = e2e_ms <= serial_ms
     best_ms = e2e_ms if pipelined else serial_ms
     e2e = {"value": P / (best_ms * 1e-3), "unit": UNIT,

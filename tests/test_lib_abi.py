@@ -203,3 +203,26 @@ def test_staging_copy_is_exact_at_every_alignment_and_size():
             fn(dst.ctypes.data + do, src.ctypes.data + so, n)
             assert np.array_equal(dst[do:do + n], src[so:so + n]), (n, so, do)
             assert not dst[:do].any() and not dst[do + n:].any(), (n, so, do)
+
+
+def test_c_caller_compiles_against_the_header_and_links(tmp_path):
+    # The header is the binding's source of truth for Go / Rust / Java: it
+    # must compile as strict C11, and a C program must link and call the
+    # library (entry points that need no GPU).
+    import shutil
+    import subprocess
+
+    from slmopt import build
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lib = _lib.library_path()
+    exe = tmp_path / "abi_caller"
+    src = Path(__file__).with_name("abi_caller.c")
+    cmd = [gcc, "-std=c11", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", str(build.INCLUDE),
+           str(src), "-o", str(exe), str(lib), f"-Wl,-rpath,{lib.parent}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0 and run.stdout.strip().endswith("ok"), run.stdout + run.stderr
